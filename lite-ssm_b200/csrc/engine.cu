@@ -1,0 +1,847 @@
+// engine.cu — the model driver above the ops: .ssm loading to HBM, seeded synthetic
+// models, sessions (recurrent state + workspace for `batch` sequences), prefill,
+// CUDA-graph decode and greedy generation. Restates the sequence of
+// src/model/mamba2_block.cpp:51-327, src/model/mamba2_model.cpp:62-211 and
+// src/runtime/inference.cpp:14-70 with B200-first changes:
+//   * the weights image is copied to HBM once (no unified memory on x86 + B200);
+//   * in_proj is ONE GEMM/GEMV over all [z | xBC | dt] rows (the reference runs three
+//     row slices of the same weight, mamba2_block.cpp:150-152: identical products);
+//   * decode fuses RMSNorm into the GEMV prologue, conv-update + SiLU + split into one
+//     kernel, the mixer gate into ssd_step, the residual add into the out_proj
+//     epilogue, and argmax + next embedding gather into one kernel; the whole decode
+//     step is captured once in a CUDA graph and replayed per token, with the greedy
+//     token staying on the device (only the generated ids come back at the end).
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <sstream>
+
+#include "device_util.cuh"
+#include "lssm_internal.h"
+#include "ssm_format.h"
+#include "synth_rng.h"
+
+namespace lssm {
+
+cudaError_t launch_gemv_int4_ex(const void* x, const void* packed, const void* scales, void* y, uint32_t M,
+                                uint32_t N, uint32_t K, const void* norm_w, float eps, int epilogue, cudaStream_t s);
+cudaError_t launch_embed_gather(const uint32_t* tokens, const void* embed, void* hidden, uint32_t rows,
+                                uint32_t d_model, uint32_t vocab, int* err, cudaStream_t s);
+cudaError_t launch_conv_silu_split(const void* xbc, uint64_t in_stride, const void* w, const void* bias, void* xo,
+                                   void* bo, void* co, uint32_t B, uint32_t L, uint32_t d_inner, uint32_t GN,
+                                   uint32_t K, cudaStream_t s);
+cudaError_t launch_conv_update_silu_split(const void* xbc, uint64_t in_stride, void* state, const void* w,
+                                          const void* bias, void* xo, void* bo, void* co, uint32_t B, uint32_t d_inner,
+                                          uint32_t GN, uint32_t K, cudaStream_t s);
+cudaError_t launch_seed_strided(const void* xbc, uint64_t in_stride, void* state, uint32_t B, uint32_t L, uint32_t D,
+                                uint32_t K, cudaStream_t s);
+cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
+                        cudaStream_t s);
+cudaError_t launch_argmax_pick(const void* logits, uint32_t B, uint32_t V, uint32_t* cur, uint32_t* history,
+                               uint32_t hist_stride, uint32_t* step, const void* embed, void* hidden, uint32_t d_model,
+                               cudaStream_t s);
+cudaError_t launch_synth_f16(void* out, uint64_t n, uint64_t seed, uint64_t stream, float amp, cudaStream_t s);
+cudaError_t launch_synth_int4(void* out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream, float amp,
+                              cudaStream_t s);
+
+int* tc_error_word();
+
+// ---------------------------------------------------------------------------
+//  .ssm parse / plan
+// ---------------------------------------------------------------------------
+std::string ssm_parse(const uint8_t* base, size_t size, SsmImage* out) {
+    if (size < sizeof(SsmHeader))
+        return "SSMFile: file too small to contain a header (" + std::to_string(size) + " bytes)";
+    SsmHeader h;
+    std::memcpy(&h, base, sizeof(h));
+    if (std::memcmp(h.magic, "LSSM", 4) != 0) return "SSMFile: bad magic; not a .ssm file";
+    if (h.version != SSM_VERSION) return "SSMFile: unsupported version " + std::to_string(h.version);
+    if (h.header_size != sizeof(SsmHeader)) return "SSMFile: header_size mismatch";
+    if (h.index_offset < sizeof(SsmHeader) || h.index_offset > size || h.data_offset < h.index_offset ||
+        h.data_offset > size)
+        return "SSMFile: index/data offsets out of range";
+    if (h.n_groups == 0) h.n_groups = 1;   // pre-group files (ssm_loader.cpp:40)
+    out->hdr = h;
+    out->order.clear();
+    out->by_name.clear();
+    size_t cur = h.index_offset;
+    for (uint32_t i = 0; i < h.n_tensors; ++i) {
+        if (cur + sizeof(SsmIndexPrefix) > size) return "SSMFile: out-of-bounds read while parsing tensor index prefix";
+        SsmIndexPrefix p;
+        std::memcpy(&p, base + cur, sizeof(p));
+        cur += sizeof(p);
+        if (p.rank == 0 || p.rank > 4)
+            return "SSMFile: tensor " + std::to_string(i) + " has unsupported rank " + std::to_string(p.rank);
+        if (cur + 8ull * p.rank > size) return "SSMFile: out-of-bounds read while parsing tensor shape";
+        TensorRec t;
+        t.dtype = p.dtype;
+        t.rank = p.rank;
+        t.offset = p.offset;
+        t.nbytes = p.nbytes;
+        std::memcpy(t.shape, base + cur, 8ull * p.rank);
+        cur += 8ull * p.rank;
+        if (cur + p.name_len > size) return "SSMFile: out-of-bounds read while parsing tensor name";
+        t.name.assign(reinterpret_cast<const char*>(base + cur), p.name_len);
+        cur += p.name_len;
+        const size_t raw = sizeof(p) + 8ull * p.rank + p.name_len;
+        cur += align_up(raw, 8) - raw;
+        if (t.offset + t.nbytes > size) return "SSMFile: payload for '" + t.name + "' overflows file";
+        if (p.dtype > DT_INT4_B32) return "SSMFile: '" + t.name + "' has unknown dtype";
+        const size_t expect = packed_nbytes(t.dtype, t.numel());
+        if (expect != t.nbytes)
+            return "SSMFile: '" + t.name + "' nbytes=" + std::to_string(t.nbytes) + " but expected packed=" +
+                   std::to_string(expect);
+        if (out->by_name.count(t.name)) return "SSMFile: duplicate tensor name in index";
+        out->by_name[t.name] = out->order.size();
+        out->order.push_back(std::move(t));
+        if (cur > h.data_offset) return "SSMFile: index walk overran data_offset";
+    }
+    return "";
+}
+
+std::vector<uint8_t> ssm_plan(const SsmHeader& hp, std::vector<TensorRec>& tensors, uint64_t* data_offset) {
+    size_t index_size = 0;
+    for (auto& t : tensors) index_size += align_up(sizeof(SsmIndexPrefix) + 8ull * t.rank + t.name.size(), 8);
+    const uint64_t index_offset = sizeof(SsmHeader);
+    const uint64_t doff = align_up(index_offset + index_size, SSM_ALIGN);
+    uint64_t cursor = doff;
+    for (auto& t : tensors) {
+        t.nbytes = packed_nbytes(t.dtype, t.numel());
+        t.offset = cursor;
+        cursor = align_up(cursor + t.nbytes, SSM_ALIGN);
+    }
+    SsmHeader h = hp;
+    std::memcpy(h.magic, "LSSM", 4);
+    h.version = SSM_VERSION;
+    h.header_size = sizeof(SsmHeader);
+    h.n_tensors = (uint32_t)tensors.size();
+    h.index_offset = index_offset;
+    h.data_offset = doff;
+    std::memset(h.reserved, 0, sizeof(h.reserved));
+    std::vector<uint8_t> out(sizeof(SsmHeader) + index_size, 0);
+    std::memcpy(out.data(), &h, sizeof(h));
+    size_t pos = sizeof(SsmHeader);
+    for (auto& t : tensors) {
+        SsmIndexPrefix p{(uint32_t)t.name.size(), t.rank, t.dtype, 0, t.offset, t.nbytes};
+        std::memcpy(out.data() + pos, &p, sizeof(p));
+        pos += sizeof(p);
+        std::memcpy(out.data() + pos, t.shape, 8ull * t.rank);
+        pos += 8ull * t.rank;
+        std::memcpy(out.data() + pos, t.name.data(), t.name.size());
+        pos += t.name.size();
+        pos = align_up(pos, 8);
+    }
+    *data_offset = doff;
+    return out;
+}
+
+}  // namespace lssm
+
+using namespace lssm;
+
+// ---------------------------------------------------------------------------
+//  Model
+// ---------------------------------------------------------------------------
+struct LayerW {
+    const TensorRec *norm, *in_proj, *conv_w, *conv_b, *dt_bias, *A_log, *D, *mixer_norm, *out_proj;
+};
+
+struct lssm_model {
+    lssm_ctx* ctx = nullptr;
+    SsmImage img;
+    std::vector<uint8_t> head;       // header + index bytes (for save)
+    uint8_t* d_base = nullptr;       // whole .ssm image in HBM (file offsets valid)
+    size_t nbytes = 0;
+    std::vector<LayerW> layers;
+    const TensorRec *embed = nullptr, *norm_f = nullptr, *lm_head = nullptr;
+    uint32_t d_inner = 0, xbc = 0, proj = 0, GN = 0;
+};
+
+static lssm_status bind_model(lssm_model* m) {
+    auto& im = m->img;
+    auto& h = im.hdr;
+    auto need = [&](const std::string& n, const TensorRec** out) -> lssm_status {
+        *out = im.find(n);
+        if (!*out) return fail(LSSM_ERR_NOT_FOUND, "Mamba2Model: missing tensor '%s'", n.c_str());
+        return LSSM_OK;
+    };
+    if (lssm_status st = need("backbone.embeddings.weight", &m->embed)) return st;
+    if (lssm_status st = need("backbone.norm_f.weight", &m->norm_f)) return st;
+    m->lm_head = im.find("lm_head.weight");
+    if (!m->lm_head) m->lm_head = m->embed;
+    m->d_inner = h.expand * h.d_model;
+    m->GN = h.n_groups * h.d_state;
+    m->xbc = m->d_inner + 2 * m->GN;
+    m->proj = m->d_inner + m->xbc + h.n_heads;
+    if (h.n_heads * h.d_head != m->d_inner)
+        return fail(LSSM_ERR_FORMAT, "Mamba2Model: n_heads * d_head != expand * d_model");
+    if (h.n_heads % h.n_groups != 0) return fail(LSSM_ERR_FORMAT, "Mamba2Model: n_heads not divisible by n_groups");
+    m->layers.resize(h.n_layer);
+    for (uint32_t i = 0; i < h.n_layer; ++i) {
+        const std::string p = "backbone.layers." + std::to_string(i) + ".";
+        LayerW& L = m->layers[i];
+        if (lssm_status st = need(p + "norm.weight", &L.norm)) return st;
+        if (lssm_status st = need(p + "mixer.in_proj.weight", &L.in_proj)) return st;
+        if (lssm_status st = need(p + "mixer.conv1d.weight", &L.conv_w)) return st;
+        if (lssm_status st = need(p + "mixer.conv1d.bias", &L.conv_b)) return st;
+        if (lssm_status st = need(p + "mixer.dt_bias", &L.dt_bias)) return st;
+        if (lssm_status st = need(p + "mixer.A_log", &L.A_log)) return st;
+        if (lssm_status st = need(p + "mixer.D", &L.D)) return st;
+        if (lssm_status st = need(p + "mixer.norm.weight", &L.mixer_norm)) return st;
+        if (lssm_status st = need(p + "mixer.out_proj.weight", &L.out_proj)) return st;
+        if (L.in_proj->shape[0] != m->proj)
+            return fail(LSSM_ERR_FORMAT, "Mamba2Model: in_proj output dim mismatch vs config (got %llu, expected %u)",
+                        (unsigned long long)L.in_proj->shape[0], m->proj);
+        if (L.conv_w->shape[0] != m->xbc) return fail(LSSM_ERR_FORMAT, "Mamba2Model: conv1d weight dim mismatch vs config");
+        for (const TensorRec* t : {L.norm, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.D, L.mixer_norm})
+            if (t->dtype != DT_F16)
+                return fail(LSSM_ERR_FORMAT, "Mamba2Model: '%s' must be f16 (got dtype %u)", t->name.c_str(), t->dtype);
+        for (const TensorRec* t : {L.in_proj, L.out_proj})
+            if (t->dtype != DT_F16 && t->dtype != DT_INT4_B32)
+                return fail(LSSM_ERR_FORMAT, "Mamba2Model: '%s' must be f16 or int4_b32", t->name.c_str());
+    }
+    if (m->embed->dtype != DT_F16 || m->norm_f->dtype != DT_F16)
+        return fail(LSSM_ERR_FORMAT, "Mamba2Model: embeddings / norm_f must be f16");
+    if (m->lm_head->dtype != DT_F16 && m->lm_head->dtype != DT_INT4_B32)
+        return fail(LSSM_ERR_FORMAT, "Mamba2Model: lm_head must be f16 or int4_b32");
+    return LSSM_OK;
+}
+
+static lssm_status upload_image(lssm_ctx* ctx, lssm_model* m, const uint8_t* bytes, size_t n) {
+    cudaError_t e = cudaMalloc(&m->d_base, n);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_load: weights arena");
+    m->nbytes = n;
+    // Stage through pinned memory in 64 MiB pieces so the copy runs at PCIe speed.
+    const size_t piece = 64ull << 20;
+    void* pinned = nullptr;
+    if (cudaMallocHost(&pinned, piece) != cudaSuccess) pinned = nullptr;
+    for (size_t off = 0; off < n; off += piece) {
+        const size_t len = std::min(piece, n - off);
+        if (pinned) {
+            std::memcpy(pinned, bytes + off, len);
+            e = cudaMemcpyAsync(m->d_base + off, pinned, len, cudaMemcpyHostToDevice, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        } else {
+            e = cudaMemcpy(m->d_base + off, bytes + off, len, cudaMemcpyHostToDevice);
+        }
+        if (e != cudaSuccess) break;
+    }
+    if (pinned) cudaFreeHost(pinned);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_load: upload");
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_model_load_bytes(lssm_ctx* ctx, const void* bytes, size_t nbytes, lssm_model** out) {
+    if (!ctx || !bytes || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_load_bytes: null argument");
+    cudaSetDevice(ctx->device);
+    *out = nullptr;
+    std::unique_ptr<lssm_model> m(new lssm_model());
+    m->ctx = ctx;
+    const uint8_t* b = static_cast<const uint8_t*>(bytes);
+    std::string err = ssm_parse(b, nbytes, &m->img);
+    if (!err.empty()) return fail(LSSM_ERR_FORMAT, "%s", err.c_str());
+    m->head.assign(b, b + m->img.hdr.data_offset);
+    if (lssm_status st = bind_model(m.get())) return st;
+    if (lssm_status st = upload_image(ctx, m.get(), b, nbytes)) return st;
+    *out = m.release();
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_model_load(lssm_ctx* ctx, const char* path, lssm_model** out) {
+    if (!ctx || !path || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_load: null argument");
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) return fail(LSSM_ERR_INVALID_ARGUMENT, "MmapFile: cannot open '%s'", path);
+    const std::streamsize n = f.tellg();
+    f.seekg(0);
+    std::vector<uint8_t> buf((size_t)n);
+    if (n > 0 && !f.read(reinterpret_cast<char*>(buf.data()), n)) return fail(LSSM_ERR_FORMAT, "cannot read '%s'", path);
+    return lssm_model_load_bytes(ctx, buf.data(), buf.size(), out);
+}
+
+// Tensor list of a Mamba2ForCausalLM state_dict, in its order (the order the
+// reference exporter writes, tools/export_mamba2.py:162-195).
+static std::vector<TensorRec> mamba2_tensor_list(const lssm_hparams& hp, int int4) {
+    std::vector<TensorRec> v;
+    auto add = [&](const std::string& n, uint32_t dt, std::initializer_list<uint64_t> shp) {
+        TensorRec t;
+        t.name = n;
+        t.dtype = dt;
+        t.rank = (uint32_t)shp.size();
+        int i = 0;
+        for (auto s : shp) t.shape[i++] = s;
+        v.push_back(t);
+    };
+    const uint64_t di = (uint64_t)hp.expand * hp.d_model, G = hp.n_groups ? hp.n_groups : 1;
+    const uint64_t xd = di + 2 * G * hp.d_state, proj = di + xd + hp.n_heads;
+    const uint32_t lin = int4 ? DT_INT4_B32 : DT_F16;
+    add("backbone.embeddings.weight", DT_F16, {hp.vocab_size, hp.d_model});
+    for (uint32_t i = 0; i < hp.n_layer; ++i) {
+        const std::string p = "backbone.layers." + std::to_string(i) + ".";
+        add(p + "norm.weight", DT_F16, {hp.d_model});
+        add(p + "mixer.dt_bias", DT_F16, {hp.n_heads});
+        add(p + "mixer.A_log", DT_F16, {hp.n_heads});
+        add(p + "mixer.D", DT_F16, {hp.n_heads});
+        add(p + "mixer.conv1d.weight", DT_F16, {xd, 1, hp.d_conv});
+        add(p + "mixer.conv1d.bias", DT_F16, {xd});
+        add(p + "mixer.in_proj.weight", (hp.d_model % 32 == 0) ? lin : DT_F16, {proj, hp.d_model});
+        add(p + "mixer.norm.weight", DT_F16, {di});
+        add(p + "mixer.out_proj.weight", (di % 32 == 0) ? lin : DT_F16, {hp.d_model, di});
+    }
+    add("backbone.norm_f.weight", DT_F16, {hp.d_model});
+    add("lm_head.weight", DT_F16, {hp.vocab_size, hp.d_model});
+    return v;
+}
+
+static uint16_t host_f2h(float f) {
+    __half h = __float2half_rn(f);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Small per-head / per-channel vectors are made on the host in double precision and
+// rounded once to fp16 (identical on every machine with the same libm).
+//   A_log  = log(1 + 15 u)            (A = -exp(A_log) in [-16, -1])
+//   dt_bias = dt + log(-expm1(-dt)),  dt = exp(log(1e-3) + u log(100))  (inverse softplus)
+//   D = 0.5 + u;   norm weights = 0.9 + 0.2 u
+static void host_vector(const std::string& kind, uint64_t seed, uint64_t stream, uint64_t n, uint16_t* out) {
+    for (uint64_t i = 0; i < n; ++i) {
+        const double u = 0.5 * ((double)synth_value(seed, stream, i, 1.0f) + 1.0);
+        double v;
+        if (kind == "A_log") v = std::log(1.0 + 15.0 * u);
+        else if (kind == "dt_bias") {
+            const double dt = std::exp(std::log(1e-3) + u * std::log(100.0));
+            v = dt + std::log(-std::expm1(-dt));
+        } else if (kind == "D") v = 0.5 + u;
+        else v = 0.9 + 0.2 * u;   // norm weights
+        out[i] = host_f2h((float)v);
+    }
+}
+
+extern "C" lssm_status lssm_model_synthesize(lssm_ctx* ctx, const lssm_hparams* hpp, uint64_t seed, int int4,
+                                             lssm_model** out) {
+    if (!ctx || !hpp || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_synthesize: null argument");
+    cudaSetDevice(ctx->device);
+    *out = nullptr;
+    lssm_hparams hp = *hpp;
+    if (hp.n_groups == 0) hp.n_groups = 1;
+    if (!hp.d_model || !hp.n_layer || !hp.d_state || !hp.d_conv || !hp.expand || !hp.vocab_size || !hp.n_heads ||
+        !hp.d_head)
+        return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_synthesize: zero hyperparameter");
+    std::unique_ptr<lssm_model> m(new lssm_model());
+    m->ctx = ctx;
+    std::vector<TensorRec> ts = mamba2_tensor_list(hp, int4);
+    SsmHeader h{};
+    h.d_model = hp.d_model; h.n_layer = hp.n_layer; h.d_state = hp.d_state; h.d_conv = hp.d_conv;
+    h.expand = hp.expand; h.vocab_size = hp.vocab_size; h.n_heads = hp.n_heads; h.d_head = hp.d_head;
+    h.chunk_size = hp.chunk_size ? hp.chunk_size : 256; h.default_dtype = DT_F16; h.n_groups = hp.n_groups;
+    h.norm_before_gate = hp.norm_before_gate;
+    uint64_t doff = 0;
+    m->head = ssm_plan(h, ts, &doff);
+    const size_t total = align_up(ts.back().offset + ts.back().nbytes, SSM_ALIGN);
+    std::string err = ssm_parse(m->head.data(), m->head.size(), &m->img);
+    // The header alone is shorter than the payload offsets; re-parse against the full size.
+    {
+        std::vector<uint8_t> probe(m->head);
+        SsmImage im;
+        im.hdr = *reinterpret_cast<const SsmHeader*>(probe.data());
+        for (size_t i = 0; i < ts.size(); ++i) { im.by_name[ts[i].name] = i; im.order.push_back(ts[i]); }
+        m->img = std::move(im);
+    }
+    (void)err;
+    if (lssm_status st = bind_model(m.get())) return st;
+    cudaError_t e = cudaMalloc(&m->d_base, total);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_synthesize: weights arena");
+    m->nbytes = total;
+    e = cudaMemsetAsync(m->d_base, 0, total, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_base, m->head.data(), m->head.size(), cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_synthesize");
+    const double inv_sqrt3 = 1.7320508075688772;
+    std::vector<uint16_t> hv;
+    for (size_t i = 0; i < ts.size(); ++i) {
+        const TensorRec& t = m->img.order[i];
+        const uint64_t stream = i + 1;
+        uint8_t* dst = m->d_base + t.offset;
+        const std::string& n = t.name;
+        auto ends = [&](const char* s) { return n.size() >= strlen(s) && n.compare(n.size() - strlen(s), strlen(s), s) == 0; };
+        if (ends("embeddings.weight") || n == "lm_head.weight") {
+            // lm_head is tied to the embeddings (same stream => same values)
+            const uint64_t st = (n == "lm_head.weight") ? 1 : stream;
+            e = launch_synth_f16(dst, t.numel(), seed, st, (float)(0.5 * inv_sqrt3), ctx->stream);
+        } else if (ends("in_proj.weight") || ends("out_proj.weight")) {
+            const float amp = (float)(inv_sqrt3 / std::sqrt((double)t.shape[1]));
+            if (t.dtype == DT_INT4_B32)
+                e = launch_synth_int4(dst, (uint32_t)t.shape[0], (uint32_t)t.shape[1], seed, stream, amp, ctx->stream);
+            else
+                e = launch_synth_f16(dst, t.numel(), seed, stream, amp, ctx->stream);
+        } else if (ends("conv1d.weight") || ends("conv1d.bias")) {
+            e = launch_synth_f16(dst, t.numel(), seed, stream, 0.5f, ctx->stream);
+        } else {
+            hv.resize(t.numel());
+            const char* kind = ends("A_log") ? "A_log" : ends("dt_bias") ? "dt_bias" : ends(".D") ? "D" : "norm";
+            host_vector(kind, seed, stream, t.numel(), hv.data());
+            e = cudaMemcpyAsync(dst, hv.data(), t.nbytes, cudaMemcpyHostToDevice, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "lssm_model_synthesize: fill");
+    }
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_synthesize");
+    *out = m.release();
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_model_save(lssm_model* m, const char* path) {
+    if (!m || !path) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_save: null argument");
+    cudaSetDevice(m->ctx->device);
+    std::vector<uint8_t> host(m->nbytes);
+    cudaError_t e = cudaMemcpy(host.data(), m->d_base, m->nbytes, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "lssm_model_save");
+    std::memcpy(host.data(), m->head.data(), m->head.size());
+    std::ofstream f(path, std::ios::binary);
+    if (!f) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_save: cannot open '%s'", path);
+    f.write(reinterpret_cast<const char*>(host.data()), (std::streamsize)host.size());
+    return f ? LSSM_OK : fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_save: write failed");
+}
+
+extern "C" lssm_status lssm_model_config(const lssm_model* m, lssm_hparams* o) {
+    if (!m || !o) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_config: null argument");
+    const SsmHeader& h = m->img.hdr;
+    *o = lssm_hparams{h.d_model, h.n_layer, h.d_state, h.d_conv, h.expand, h.vocab_size, h.n_heads, h.d_head,
+                      h.chunk_size, h.default_dtype, h.n_groups, h.norm_before_gate};
+    return LSSM_OK;
+}
+
+extern "C" size_t lssm_model_nbytes(const lssm_model* m) { return m ? m->nbytes : 0; }
+extern "C" const void* lssm_model_device_base(const lssm_model* m) { return m ? m->d_base : nullptr; }
+
+extern "C" lssm_status lssm_model_tensor(const lssm_model* m, const char* name, uint64_t* offset, uint64_t* nbytes,
+                                         uint32_t* dtype) {
+    if (!m || !name) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_tensor: null argument");
+    const TensorRec* t = m->img.find(name);
+    if (!t) return fail(LSSM_ERR_NOT_FOUND, "SSMFile: no tensor named '%s'", name);
+    if (offset) *offset = t->offset;
+    if (nbytes) *nbytes = t->nbytes;
+    if (dtype) *dtype = t->dtype;
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_model_destroy(lssm_model* m) {
+    if (!m) return LSSM_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->d_base) cudaFree(m->d_base);
+    delete m;
+    return LSSM_OK;
+}
+
+// Host-only planner export (format tests run it without a GPU).
+extern "C" size_t lssm_plan_layout(const lssm_hparams* hp, int int4, void* out, size_t cap, uint64_t* data_offset,
+                                   uint64_t* total_bytes) {
+    std::vector<TensorRec> ts = mamba2_tensor_list(*hp, int4);
+    SsmHeader h{};
+    h.d_model = hp->d_model; h.n_layer = hp->n_layer; h.d_state = hp->d_state; h.d_conv = hp->d_conv;
+    h.expand = hp->expand; h.vocab_size = hp->vocab_size; h.n_heads = hp->n_heads; h.d_head = hp->d_head;
+    h.chunk_size = hp->chunk_size; h.default_dtype = DT_F16; h.n_groups = hp->n_groups ? hp->n_groups : 1;
+    h.norm_before_gate = hp->norm_before_gate;
+    uint64_t doff = 0;
+    std::vector<uint8_t> b = ssm_plan(h, ts, &doff);
+    if (data_offset) *data_offset = doff;
+    if (total_bytes) *total_bytes = align_up(ts.back().offset + ts.back().nbytes, SSM_ALIGN);
+    if (out && cap >= b.size()) std::memcpy(out, b.data(), b.size());
+    return b.size();
+}
+
+// Host-only parser export: returns 0 and fills hparams on success, else copies the
+// loader's message into `err` (the same messages as src/core/ssm_loader.cpp).
+extern "C" int lssm_parse_header(const void* bytes, size_t n, lssm_hparams* hp, uint32_t* n_tensors, char* err,
+                                 size_t err_cap) {
+    SsmImage im;
+    std::string e = ssm_parse(static_cast<const uint8_t*>(bytes), n, &im);
+    if (!e.empty()) {
+        if (err && err_cap) { std::strncpy(err, e.c_str(), err_cap - 1); err[err_cap - 1] = 0; }
+        return 1;
+    }
+    const SsmHeader& h = im.hdr;
+    if (hp) *hp = lssm_hparams{h.d_model, h.n_layer, h.d_state, h.d_conv, h.expand, h.vocab_size, h.n_heads,
+                               h.d_head, h.chunk_size, h.default_dtype, h.n_groups, h.norm_before_gate};
+    if (n_tensors) *n_tensors = h.n_tensors;
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+//  Session
+// ---------------------------------------------------------------------------
+struct lssm_session {
+    lssm_ctx* ctx = nullptr;
+    lssm_model* m = nullptr;
+    uint32_t batch = 0, max_L = 0;
+    // state
+    uint8_t* conv = nullptr;   // per layer (batch, xbc, d_conv) fp16
+    float* ssd = nullptr;      // per layer (batch, H, P, N) fp32
+    size_t conv_layer = 0, ssd_layer = 0;   // elements per layer
+    // workspace (rows = batch * max_L)
+    __half *hidden = nullptr, *normed = nullptr, *proj = nullptr, *xs = nullptr, *Bs = nullptr, *Cs = nullptr,
+           *ys = nullptr, *gated = nullptr, *mixn = nullptr, *bout = nullptr, *logits = nullptr, *lastrows = nullptr;
+    __half* wscratch = nullptr;   // dequantised INT4 weight for the prefill GEMM
+    size_t wscratch_elems = 0;
+    uint32_t *d_tokens = nullptr, *d_cur = nullptr, *d_hist = nullptr, *d_step = nullptr;
+    uint32_t hist_cap = 0;
+    int* d_err = nullptr;
+    cudaEvent_t ev[4] = {};
+    float prefill_ms = 0.0f, decode_ms = 0.0f;
+    bool use_graph = true;
+    cudaGraphExec_t graph = nullptr;
+    bool logits_valid = false;
+};
+
+static lssm_status s_alloc(void** p, size_t n, const char* what) {
+    cudaError_t e = cudaMalloc(p, n ? n : 16);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
+    if (!s) return LSSM_OK;
+    cudaSetDevice(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
+                  s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err};
+    for (void* p : ps)
+        if (p) cudaFree(p);
+    for (auto& e : s->ev)
+        if (e) cudaEventDestroy(e);
+    delete s;
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_t batch, uint32_t max_L,
+                                           lssm_session** out) {
+    if (!ctx || !m || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: null argument");
+    if (batch == 0 || max_L == 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: batch and max_seq_len must be >= 1");
+    cudaSetDevice(ctx->device);
+    *out = nullptr;
+    std::unique_ptr<lssm_session, lssm_status (*)(lssm_session*)> s(new lssm_session(), lssm_session_destroy);
+    s->ctx = ctx;
+    s->m = m;
+    s->batch = batch;
+    s->max_L = max_L;
+    const SsmHeader& h = m->img.hdr;
+    const size_t rows = (size_t)batch * max_L;
+    s->conv_layer = (size_t)batch * m->xbc * h.d_conv;
+    s->ssd_layer = (size_t)batch * h.n_heads * h.d_head * h.d_state;
+    lssm_status st;
+#define SA(ptr, n, what) if ((st = s_alloc(reinterpret_cast<void**>(&ptr), n, what))) return st
+    SA(s->conv, s->conv_layer * h.n_layer * 2, "session: conv state");
+    SA(s->ssd, s->ssd_layer * h.n_layer * 4, "session: ssd state");
+    SA(s->hidden, rows * h.d_model * 2, "session: hidden");
+    SA(s->normed, rows * h.d_model * 2, "session: normed");
+    SA(s->proj, rows * m->proj * 2, "session: proj");
+    SA(s->xs, rows * m->d_inner * 2, "session: x");
+    SA(s->Bs, rows * m->GN * 2, "session: B");
+    SA(s->Cs, rows * m->GN * 2, "session: C");
+    SA(s->ys, rows * m->d_inner * 2, "session: y");
+    SA(s->gated, rows * m->d_inner * 2, "session: gated");
+    SA(s->mixn, rows * m->d_inner * 2, "session: mixer norm");
+    SA(s->bout, rows * h.d_model * 2, "session: block out");
+    SA(s->logits, (size_t)batch * h.vocab_size * 2, "session: logits");
+    SA(s->lastrows, (size_t)batch * h.d_model * 2, "session: last rows");
+    SA(s->d_tokens, rows * 4, "session: tokens");
+    SA(s->d_cur, (size_t)batch * 4, "session: current tokens");
+    SA(s->d_step, 16, "session: step");
+    SA(s->d_err, 16, "session: error word");
+    bool any_int4 = false;
+    size_t wmax = 0;
+    for (auto& L : m->layers) {
+        if (L.in_proj->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)m->proj * h.d_model); }
+        if (L.out_proj->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.d_model * m->d_inner); }
+    }
+    if (m->lm_head->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.vocab_size * h.d_model); }
+    if (any_int4) {
+        SA(s->wscratch, wmax * 2, "session: dequant scratch");
+        s->wscratch_elems = wmax;
+    }
+#undef SA
+    for (auto& e : s->ev) cudaEventCreate(&e);
+    cudaMemsetAsync(s->d_err, 0, 16, ctx->stream);
+    if ((st = lssm_session_reset(s.get()))) return st;
+    *out = s.release();
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_reset(lssm_session* s) {
+    if (!s) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_reset: null session");
+    cudaSetDevice(s->ctx->device);
+    const SsmHeader& h = s->m->img.hdr;
+    cudaError_t e = cudaMemsetAsync(s->conv, 0, s->conv_layer * h.n_layer * 2, s->ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->ssd, 0, s->ssd_layer * h.n_layer * 4, s->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "Mamba2State::reset");
+    s->logits_valid = false;
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t value) {
+    if (!s || !key) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_set_option: null argument");
+    if (std::strcmp(key, "cuda_graph") == 0) {
+        s->use_graph = value != 0;
+        if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+        return LSSM_OK;
+    }
+    return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_set_option: unknown key '%s'", key);
+}
+
+#define CU(expr)                                                  \
+    do {                                                          \
+        cudaError_t _e = (expr);                                  \
+        if (_e != cudaSuccess) return cuda_fail(_e, #expr);       \
+    } while (0)
+
+static inline const void* W(const lssm_model* m, const TensorRec* t) { return m->d_base + t->offset; }
+
+// Linear over `rows` activation rows with a .ssm weight (f16 or INT4_B32): Y = X W^T.
+// rows <= 8 uses the GEMV kernels (optionally with fused RMSNorm / residual),
+// otherwise the tensor-core GEMM (INT4 dequantised to fp16 scratch first).
+static lssm_status linear(lssm_session* s, const TensorRec* w, const __half* x, __half* y, uint32_t rows, uint32_t N,
+                          uint32_t K, const TensorRec* prenorm, int epilogue, cudaStream_t st) {
+    const lssm_model* m = s->m;
+    const void* wp = W(m, w);
+    if (rows <= 8) {
+        const void* nw = prenorm ? W(m, prenorm) : nullptr;
+        if (w->dtype == DT_INT4_B32)
+            CU(launch_gemv_int4_ex(x, wp, static_cast<const uint8_t*>(wp) + (size_t)N * K / 2, y, rows, N, K, nw, 1e-5f,
+                                   epilogue, st));
+        else
+            CU(launch_gemv_f16(x, wp, y, rows, N, K, nw, 1e-5f, epilogue, st));
+        return LSSM_OK;
+    }
+    const __half* xin = x;
+    if (prenorm) {
+        CU(launch_rmsnorm_f16(x, W(m, prenorm), s->normed, rows, K, 1e-5f, st));
+        xin = s->normed;
+    }
+    const void* wf = wp;
+    if (w->dtype == DT_INT4_B32) {
+        CU(launch_int4_dequant_f16(wp, static_cast<const uint8_t*>(wp) + (size_t)N * K / 2, s->wscratch, N, K, st));
+        wf = s->wscratch;
+    }
+    if (epilogue == 2) {
+        CU(launch_gemm_f16(xin, wf, s->bout, rows, N, K, 0, st));
+        CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
+    } else {
+        CU(launch_gemm_f16(xin, wf, y, rows, N, K, epilogue, st));
+    }
+    return LSSM_OK;
+}
+
+// One Mamba-2 block over rows = batch * L activation rows (decode: L == 1).
+static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool decode, cudaStream_t st) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    const LayerW& lw = m->layers[layer];
+    const uint32_t B = s->batch, rows = B * L, dm = h.d_model, di = m->d_inner, GN = m->GN, xd = m->xbc,
+                   proj = m->proj, H = h.n_heads, P = h.d_head, N = h.d_state, Kc = h.d_conv;
+    __half* conv = reinterpret_cast<__half*>(s->conv) + s->conv_layer * layer;
+    float* ssd = s->ssd + s->ssd_layer * layer;
+    lssm_status r;
+    // 1+2. RMSNorm + in_proj over [z | xBC | dt]
+    if ((r = linear(s, lw.in_proj, s->hidden, s->proj, rows, proj, dm, lw.norm, 0, st))) return r;
+    const __half* zc = s->proj;
+    const __half* xbc = s->proj + di;
+    const __half* dtc = s->proj + di + xd;
+    if (decode) {
+        // 3+4. conv update + SiLU + split
+        CU(launch_conv_update_silu_split(xbc, proj, conv, W(m, lw.conv_w), W(m, lw.conv_b), s->xs, s->Bs, s->Cs, B, di,
+                                         GN, Kc, st));
+        // 5+6. ssd_step with the fused gate -> gated
+        StepArgs a{};
+        a.x = s->xs; a.B = s->Bs; a.C = s->Cs; a.dt_raw = dtc;
+        a.dt_bias = static_cast<const __half*>(W(m, lw.dt_bias));
+        a.A_log = static_cast<const __half*>(W(m, lw.A_log));
+        a.D = static_cast<const __half*>(W(m, lw.D));
+        a.state = ssd; a.y = s->gated; a.z = zc;
+        a.batch = B; a.H = H; a.P = P; a.N = N; a.G = h.n_groups;
+        a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
+        a.x_bs = di; a.bc_bs = GN; a.dt_bs = proj; a.y_bs = di; a.z_bs = proj;
+        CU(launch_ssd_step_ex(a, st));
+    } else {
+        CU(launch_conv_silu_split(xbc, proj, W(m, lw.conv_w), W(m, lw.conv_b), s->xs, s->Bs, s->Cs, B, L, di, GN, Kc, st));
+        SsdArgs a{};
+        a.X = s->xs; a.B = s->Bs; a.C = s->Cs; a.dt_raw = dtc;
+        a.dt_bias = W(m, lw.dt_bias); a.A_log = W(m, lw.A_log); a.D = W(m, lw.D);
+        a.Y = s->ys; a.state = ssd;
+        a.batch = B; a.L = L; a.H = H; a.P = P; a.N = N; a.G = h.n_groups; a.chunk = h.chunk_size;
+        a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
+        a.x_dtype = 0; a.dt_dtype = 0; a.param_dtype = 0; a.y_dtype = 0;
+        a.x_row_stride = di; a.bc_row_stride = GN; a.dt_row_stride = proj; a.y_row_stride = di;
+        CU(launch_ssd_chunked(a, st));
+        CU(launch_gate(zc, proj, s->ys, s->gated, rows, di, st));
+    }
+    // 7+8+9. gated RMSNorm + out_proj + residual add into hidden
+    if ((r = linear(s, lw.out_proj, s->gated, s->hidden, rows, dm, di, lw.mixer_norm, 2, st))) return r;
+    // 10. seed conv state from pre-conv xBC after a prefill
+    if (!decode) CU(launch_seed_strided(xbc, proj, conv, B, L, xd, Kc, st));
+    return LSSM_OK;
+}
+
+// norm_f + lm_head over `x` (batch rows, contiguous) -> logits (batch, vocab) fp16.
+static lssm_status logits_of(lssm_session* s, const __half* x, cudaStream_t st) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    for (uint32_t b0 = 0; b0 < s->batch; b0 += 8) {
+        const uint32_t r = std::min<uint32_t>(8, s->batch - b0);
+        lssm_status e = linear(s, m->lm_head, x + (size_t)b0 * h.d_model, s->logits + (size_t)b0 * h.vocab_size, r,
+                               h.vocab_size, h.d_model, m->norm_f, 0, st);
+        if (e) return e;
+    }
+    return LSSM_OK;
+}
+
+static lssm_status check_err(lssm_session* s, const char* what) {
+    int herr = 0;
+    CU(cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr == 2) {
+        cudaMemset(s->d_err, 0, sizeof(int));
+        return fail(LSSM_ERR_INVALID_ARGUMENT, "Mamba2Model::embed: token_id out of range (%s)", what);
+    }
+    int* tw = tc_error_word();
+    if (tw) {
+        CU(cudaMemcpy(&herr, tw, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr) {
+            cudaMemset(tw, 0, sizeof(int));
+            return fail(LSSM_ERR_TIMEOUT, "%s: a bounded device wait timed out", what);
+        }
+    }
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_prefill(lssm_session* s, const uint32_t* tokens, uint32_t L, uint32_t* next_tokens) {
+    if (!s || !tokens) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_prefill: null argument");
+    if (L == 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "forward_prefill: L must be >= 1");
+    if (L > s->max_L) return fail(LSSM_ERR_INVALID_ARGUMENT, "forward_prefill: L exceeds workspace max_seq_len");
+    cudaSetDevice(s->ctx->device);
+    cudaStream_t st = s->ctx->stream;
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    const uint32_t rows = s->batch * L;
+    CU(cudaEventRecord(s->ev[0], st));
+    CU(cudaMemcpyAsync(s->d_tokens, tokens, (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+    CU(launch_embed_gather(s->d_tokens, W(m, m->embed), s->hidden, rows, h.d_model, h.vocab_size, s->d_err, st));
+    for (uint32_t l = 0; l < h.n_layer; ++l)
+        if (lssm_status r = run_block(s, l, L, false, st)) return r;
+    // last row of each sequence -> contiguous (batch, d_model)
+    CU(cudaMemcpy2DAsync(s->lastrows, (size_t)h.d_model * 2, s->hidden + (size_t)(L - 1) * h.d_model,
+                         (size_t)L * h.d_model * 2, (size_t)h.d_model * 2, s->batch, cudaMemcpyDeviceToDevice, st));
+    if (lssm_status r = logits_of(s, s->lastrows, st)) return r;
+    CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, nullptr, 0, nullptr, nullptr, nullptr, 0, st));
+    CU(cudaEventRecord(s->ev[1], st));
+    if (next_tokens) CU(cudaMemcpyAsync(next_tokens, s->d_cur, (size_t)s->batch * 4, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    cudaEventElapsedTime(&s->prefill_ms, s->ev[0], s->ev[1]);
+    s->logits_valid = true;
+    return check_err(s, "prefill");
+}
+
+// One decode step on the device: input = s->hidden rows (already embedded), output:
+// logits, d_cur, history[step] and hidden = embed(next) for the following step.
+static lssm_status decode_step_body(lssm_session* s, cudaStream_t st) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    for (uint32_t l = 0; l < h.n_layer; ++l)
+        if (lssm_status r = run_block(s, l, 1, true, st)) return r;
+    if (lssm_status r = logits_of(s, s->hidden, st)) return r;
+    CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, s->d_hist, s->hist_cap, s->d_step, W(m, m->embed),
+                          s->hidden, h.d_model, st));
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint32_t n_steps, uint32_t* out_tokens) {
+    if (!s || !first) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_decode: null argument");
+    cudaSetDevice(s->ctx->device);
+    cudaStream_t st = s->ctx->stream;
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    if (n_steps == 0) return LSSM_OK;
+    if (n_steps > s->hist_cap) {
+        if (s->d_hist) cudaFree(s->d_hist);
+        s->d_hist = nullptr;
+        if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+        CU(cudaMalloc(&s->d_hist, (size_t)s->batch * n_steps * 4));
+        s->hist_cap = n_steps;
+    }
+    CU(cudaMemcpyAsync(s->d_cur, first, (size_t)s->batch * 4, cudaMemcpyHostToDevice, st));
+    CU(cudaMemsetAsync(s->d_step, 0, 4, st));
+    CU(launch_embed_gather(s->d_cur, W(m, m->embed), s->hidden, s->batch, h.d_model, h.vocab_size, s->d_err, st));
+    if (s->use_graph && !s->graph) {
+        cudaGraph_t g;
+        CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        lssm_status r = decode_step_body(s, st);
+        cudaError_t e = cudaStreamEndCapture(st, &g);
+        if (r) { if (e == cudaSuccess) cudaGraphDestroy(g); return r; }
+        if (e != cudaSuccess) return cuda_fail(e, "decode graph capture");
+        e = cudaGraphInstantiate(&s->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { s->graph = nullptr; return cuda_fail(e, "decode graph instantiate"); }
+    }
+    CU(cudaEventRecord(s->ev[2], st));
+    for (uint32_t i = 0; i < n_steps; ++i) {
+        if (s->graph) CU(cudaGraphLaunch(s->graph, st));
+        else if (lssm_status r = decode_step_body(s, st)) return r;
+    }
+    CU(cudaEventRecord(s->ev[3], st));
+    if (out_tokens) {
+        // history is (batch, hist_cap); copy the first n_steps of each row
+        CU(cudaMemcpy2DAsync(out_tokens, (size_t)n_steps * 4, s->d_hist, (size_t)s->hist_cap * 4, (size_t)n_steps * 4,
+                             s->batch, cudaMemcpyDeviceToHost, st));
+    }
+    CU(cudaStreamSynchronize(st));
+    cudaEventElapsedTime(&s->decode_ms, s->ev[2], s->ev[3]);
+    s->logits_valid = true;
+    return check_err(s, "decode");
+}
+
+extern "C" lssm_status lssm_generate(lssm_session* s, const uint32_t* prompt, uint32_t L, uint32_t max_new,
+                                     uint32_t eos, uint32_t* out, uint32_t* n_out) {
+    if (!s || !prompt || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_generate: null argument");
+    if (max_new == 0) { if (n_out) *n_out = 0; return LSSM_OK; }
+    lssm_status r = lssm_session_reset(s);
+    if (r) return r;
+    std::vector<uint32_t> first(s->batch);
+    if ((r = lssm_prefill(s, prompt, L, first.data()))) return r;
+    std::vector<uint32_t> rest((size_t)s->batch * (max_new - 1));
+    if (max_new > 1 && (r = lssm_decode(s, first.data(), max_new - 1, rest.data()))) return r;
+    uint32_t produced = max_new;
+    for (uint32_t b = 0; b < s->batch; ++b) {
+        out[(size_t)b * max_new] = first[b];
+        for (uint32_t i = 1; i < max_new; ++i) out[(size_t)b * max_new + i] = rest[(size_t)b * (max_new - 1) + i - 1];
+    }
+    if (eos != 0xFFFFFFFFu && s->batch == 1) {   // inference.cpp:56 stops after emitting eos
+        for (uint32_t i = 0; i < max_new; ++i)
+            if (out[i] == eos) { produced = i + 1; break; }
+    }
+    if (n_out) *n_out = produced;
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_logits(lssm_session* s, float* out) {
+    if (!s || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_logits: null argument");
+    if (!s->logits_valid) return fail(LSSM_ERR_STATE, "lssm_session_logits: no logits computed yet");
+    const SsmHeader& h = s->m->img.hdr;
+    const size_t n = (size_t)s->batch * h.vocab_size;
+    std::vector<uint16_t> tmp(n);
+    CU(cudaMemcpy(tmp.data(), s->logits, n * 2, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < n; ++i) {
+        __half hv = *reinterpret_cast<__half*>(&tmp[i]);
+        out[i] = __half2float(hv);
+    }
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_timing(lssm_session* s, float* prefill_ms, float* decode_ms) {
+    if (!s) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_timing: null session");
+    if (prefill_ms) *prefill_ms = s->prefill_ms;
+    if (decode_ms) *decode_ms = s->decode_ms;
+    return LSSM_OK;
+}

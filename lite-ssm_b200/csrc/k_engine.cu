@@ -1,0 +1,292 @@
+// k_engine.cu — kernels the model driver needs around the ops, replacing the host
+// work the reference does through unified memory:
+//   * embedding gather         (Mamba2Model::embed CPU memcpy, mamba2_model.cpp:128-137)
+//   * conv1d + SiLU + split     (conv1d.metal:63-137 + activations.metal:49-73, fused;
+//                                reads the xBC columns of the packed in_proj output)
+//   * mixer gate                (activations.metal:76-87 on strided z)
+//   * greedy argmax + next-step embedding gather (sampler.cpp:13-21 first-max rule,
+//     read_logits_fp32 mamba2_model.cpp:177-211 — fp16 -> fp32 is exact, so comparing
+//     fp16 values is comparing the reference's fp32 logits)
+//   * seeded synthetic weights in the .ssm payload layout (INT4_B32 packing restating
+//     tools/export_mamba2.py:68-103 bit for bit).
+#include "device_util.cuh"
+#include "lssm_internal.h"
+#include "synth_rng.h"
+
+namespace lssm {
+
+// hidden[r, :] = embed[tokens[r], :]; out-of-range ids raise *err and gather row 0.
+__global__ void k_embed_gather(const uint32_t* __restrict__ tokens, const __half* __restrict__ embed,
+                               __half* __restrict__ hidden, uint32_t rows, uint32_t d_model, uint32_t vocab,
+                               int* err) {
+    const uint32_t r = blockIdx.x;
+    if (r >= rows) return;
+    uint32_t t = tokens[r];
+    if (t >= vocab) {
+        if (threadIdx.x == 0) atomicExch(err, 2);
+        t = 0;
+    }
+    const __half* src = embed + (uint64_t)t * d_model;
+    __half* dst = hidden + (uint64_t)r * d_model;
+    for (uint32_t i = threadIdx.x; i < d_model; i += blockDim.x) dst[i] = src[i];
+}
+
+cudaError_t launch_embed_gather(const uint32_t* tokens, const void* embed, void* hidden, uint32_t rows,
+                                uint32_t d_model, uint32_t vocab, int* err, cudaStream_t s) {
+    if (!rows) return cudaSuccess;
+    k_embed_gather<<<rows, 256, 0, s>>>(tokens, static_cast<const __half*>(embed), static_cast<__half*>(hidden), rows,
+                                        d_model, vocab, err);
+    return cudaGetLastError();
+}
+
+// Prefill conv over the xBC columns of proj (B, L, proj_stride) -> SiLU -> x/B/C.
+// conv output rounded to fp16 (the reference's conv_out slot), then SiLU rounded again.
+constexpr int CT = 16;
+__global__ void k_conv_silu_split(const __half* __restrict__ xbc, uint64_t in_stride, const __half* __restrict__ w,
+                                  const __half* __restrict__ bias, __half* __restrict__ xo, __half* __restrict__ bo,
+                                  __half* __restrict__ co, uint32_t L, uint32_t d_inner, uint32_t GN, uint32_t K) {
+    const uint32_t D = d_inner + 2 * GN;
+    const uint32_t d = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t t0 = blockIdx.y * CT, b = blockIdx.z;
+    if (d >= D) return;
+    const __half* xb = xbc + (uint64_t)b * L * in_stride;
+    float wk[8], win[8];
+    for (uint32_t k = 0; k < K; ++k) wk[k] = __half2float(w[(uint64_t)d * K + k]);
+    const float bv = __half2float(bias[d]);
+    for (uint32_t k = 0; k + 1 < K; ++k) {
+        const int src = (int)t0 - (int)(K - 1) + (int)k;
+        win[k] = src >= 0 ? __half2float(xb[(uint64_t)src * in_stride + d]) : 0.0f;
+    }
+    const uint32_t tend = min(t0 + CT, L);
+    for (uint32_t t = t0; t < tend; ++t) {
+        win[K - 1] = __half2float(xb[(uint64_t)t * in_stride + d]);
+        float acc = bv;
+        for (uint32_t k = 0; k < K; ++k) acc += wk[k] * win[k];
+        const __half o = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
+        const uint64_t row = (uint64_t)b * L + t;
+        if (d < d_inner) xo[row * d_inner + d] = o;
+        else if (d < d_inner + GN) bo[row * GN + (d - d_inner)] = o;
+        else co[row * GN + (d - d_inner - GN)] = o;
+        for (uint32_t k = 0; k + 1 < K; ++k) win[k] = win[k + 1];
+    }
+}
+
+cudaError_t launch_conv_silu_split(const void* xbc, uint64_t in_stride, const void* w, const void* bias, void* xo,
+                                   void* bo, void* co, uint32_t B, uint32_t L, uint32_t d_inner, uint32_t GN,
+                                   uint32_t K, cudaStream_t s) {
+    const uint32_t D = d_inner + 2 * GN;
+    if (!B || !L || K == 0 || K > 8) return K > 8 ? cudaErrorInvalidValue : cudaSuccess;
+    dim3 grid((D + 127) / 128, (L + CT - 1) / CT, B);
+    k_conv_silu_split<<<grid, 128, 0, s>>>(static_cast<const __half*>(xbc), in_stride, static_cast<const __half*>(w),
+                                           static_cast<const __half*>(bias), static_cast<__half*>(xo),
+                                           static_cast<__half*>(bo), static_cast<__half*>(co), L, d_inner, GN, K);
+    return cudaGetLastError();
+}
+
+// Decode conv update + SiLU + split: state (B, D, K) rolled in place.
+__global__ void k_conv_update_silu_split(const __half* __restrict__ xbc, uint64_t in_stride, __half* __restrict__ state,
+                                         const __half* __restrict__ w, const __half* __restrict__ bias,
+                                         __half* __restrict__ xo, __half* __restrict__ bo, __half* __restrict__ co,
+                                         uint32_t B, uint32_t d_inner, uint32_t GN, uint32_t K) {
+    const uint32_t D = d_inner + 2 * GN;
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)B * D) return;
+    const uint32_t d = (uint32_t)(i % D), b = (uint32_t)(i / D);
+    __half* sd = state + i * K;
+    const __half* wd = w + (uint64_t)d * K;
+    float acc = __half2float(bias[d]);
+    for (uint32_t k = 0; k + 1 < K; ++k) {
+        const __half v = sd[k + 1];
+        sd[k] = v;
+        acc += __half2float(v) * __half2float(wd[k]);
+    }
+    const __half xn = xbc[(uint64_t)b * in_stride + d];
+    sd[K - 1] = xn;
+    acc += __half2float(xn) * __half2float(wd[K - 1]);
+    const __half o = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
+    if (d < d_inner) xo[(uint64_t)b * d_inner + d] = o;
+    else if (d < d_inner + GN) bo[(uint64_t)b * GN + (d - d_inner)] = o;
+    else co[(uint64_t)b * GN + (d - d_inner - GN)] = o;
+}
+
+cudaError_t launch_conv_update_silu_split(const void* xbc, uint64_t in_stride, void* state, const void* w,
+                                          const void* bias, void* xo, void* bo, void* co, uint32_t B, uint32_t d_inner,
+                                          uint32_t GN, uint32_t K, cudaStream_t s) {
+    const uint64_t n = (uint64_t)B * (d_inner + 2 * GN);
+    if (!n) return cudaSuccess;
+    k_conv_update_silu_split<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        static_cast<const __half*>(xbc), in_stride, static_cast<__half*>(state), static_cast<const __half*>(w),
+        static_cast<const __half*>(bias), static_cast<__half*>(xo), static_cast<__half*>(bo), static_cast<__half*>(co), B,
+        d_inner, GN, K);
+    return cudaGetLastError();
+}
+
+// Seed conv state (B, D, K) from the last K rows of each sequence's pre-conv xBC.
+__global__ void k_seed_strided(const __half* __restrict__ xbc, uint64_t in_stride, __half* __restrict__ state,
+                               uint32_t B, uint32_t L, uint32_t D, uint32_t K) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)B * D * K) return;
+    const uint32_t k = (uint32_t)(i % K);
+    const uint64_t bd = i / K;
+    const uint32_t d = (uint32_t)(bd % D), b = (uint32_t)(bd / D);
+    const int src = (int)L - (int)K + (int)k;
+    state[i] = src >= 0 ? xbc[((uint64_t)b * L + (uint32_t)src) * in_stride + d] : __float2half_rn(0.0f);
+}
+
+cudaError_t launch_seed_strided(const void* xbc, uint64_t in_stride, void* state, uint32_t B, uint32_t L, uint32_t D,
+                                uint32_t K, cudaStream_t s) {
+    const uint64_t n = (uint64_t)B * D * K;
+    if (!n) return cudaSuccess;
+    k_seed_strided<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const __half*>(xbc), in_stride,
+                                                              static_cast<__half*>(state), B, L, D, K);
+    return cudaGetLastError();
+}
+
+// gated[r, c] = half(silu(z[r*z_stride + c]) * y[r*d + c])
+__global__ void k_gate(const __half* __restrict__ z, uint64_t z_stride, const __half* __restrict__ y,
+                       __half* __restrict__ out, uint32_t rows, uint32_t d) {
+    const uint64_t total = (uint64_t)rows * d;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / d, c = i % d;
+        out[i] = __float2half_rn(silu(__half2float(z[r * z_stride + c])) * __half2float(y[i]));
+    }
+}
+
+cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
+                        cudaStream_t s) {
+    const uint64_t n = (uint64_t)rows * d;
+    if (!n) return cudaSuccess;
+    uint64_t g = (n + 255) / 256;
+    if (g > 148 * 32) g = 148 * 32;
+    k_gate<<<(unsigned)g, 256, 0, s>>>(static_cast<const __half*>(z), z_stride, static_cast<const __half*>(y),
+                                       static_cast<__half*>(out), rows, d);
+    return cudaGetLastError();
+}
+
+// Greedy pick per sequence (first max, NaN never wins; logits[0] NaN -> id 0 like the
+// reference loop), written to cur[b] and history[b * hist_stride + *step]; optionally
+// gathers the picked token's embedding into hidden[b] for the next decode step.
+// One CTA per sequence; thread 0 of CTA 0 advances *step after all CTAs have read it
+// (the counter is advanced by a separate single-thread kernel to avoid a race).
+__global__ void __launch_bounds__(1024) k_argmax_pick(const __half* __restrict__ logits, uint32_t V,
+                                                      uint32_t* __restrict__ cur, uint32_t* __restrict__ history,
+                                                      uint32_t hist_stride, const uint32_t* __restrict__ step,
+                                                      const __half* __restrict__ embed, __half* __restrict__ hidden,
+                                                      uint32_t d_model) {
+    __shared__ float sv[32];
+    __shared__ uint32_t si[32];
+    __shared__ uint32_t pick;
+    const uint32_t b = blockIdx.x;
+    const __half* lg = logits + (uint64_t)b * V;
+    float bv = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = __half2float(lg[i]);
+        if (v > bv) { bv = v; bi = i; }       // strict: keeps the first index within a thread
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+    __syncthreads();
+    if (wid == 0) {
+        const uint32_t nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0xFFFFFFFFu;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            const float v0 = __half2float(lg[0]);
+            uint32_t p = (bi == 0xFFFFFFFFu) ? 0u : bi;
+            if (v0 != v0) p = 0;               // NaN at index 0 never gets replaced in the reference loop
+            pick = p;
+            cur[b] = p;
+            if (history) history[(uint64_t)b * hist_stride + (step ? *step : 0)] = p;
+        }
+    }
+    __syncthreads();
+    if (embed) {
+        const __half* src = embed + (uint64_t)pick * d_model;
+        __half* dst = hidden + (uint64_t)b * d_model;
+        for (uint32_t i = threadIdx.x; i < d_model; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
+__global__ void k_step_advance(uint32_t* step) { *step += 1; }
+
+cudaError_t launch_argmax_pick(const void* logits, uint32_t B, uint32_t V, uint32_t* cur, uint32_t* history,
+                               uint32_t hist_stride, uint32_t* step, const void* embed, void* hidden, uint32_t d_model,
+                               cudaStream_t s) {
+    if (!B) return cudaSuccess;
+    k_argmax_pick<<<B, 1024, 0, s>>>(static_cast<const __half*>(logits), V, cur, history, hist_stride, step,
+                                     static_cast<const __half*>(embed), static_cast<__half*>(hidden), d_model);
+    if (step) k_step_advance<<<1, 1, 0, s>>>(step);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+//  Seeded synthetic weights (see synth_rng.h for the value recipe).
+// ---------------------------------------------------------------------------
+// fp16 tensor of n values: out[i] = half(synth_uniform(seed, stream, i) * amp)
+__global__ void k_synth_f16(__half* __restrict__ out, uint64_t n, uint64_t seed, uint64_t stream, float amp) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = __float2half_rn(synth_value(seed, stream, i, amp));
+}
+
+// INT4_B32 tensor (N, K): values as k_synth_f16 (then rounded to fp16 like the exporter's
+// t.to(float16)), quantised per 32-block: packed nibbles at out, scales at out + N*K/2.
+__global__ void k_synth_int4(uint8_t* __restrict__ out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream,
+                             float amp) {
+    const uint32_t nb = K / 32;
+    const uint64_t total = (uint64_t)N * nb;
+    __half* scales = reinterpret_cast<__half*>(out + (uint64_t)N * K / 2);
+    for (uint64_t blk = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; blk < total;
+         blk += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = blk / nb, b = blk % nb;
+        float v[32];
+        float absmax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            v[j] = __half2float(__float2half_rn(synth_value(seed, stream, row * K + b * 32 + j, amp)));
+            absmax = fmaxf(absmax, fabsf(v[j]));
+        }
+        absmax = fmaxf(absmax, 1e-12f);
+        const float scale = __fdiv_rn(absmax, 7.0f);
+        scales[blk] = __float2half_rn(scale);
+        uint8_t* dst = out + row * (K / 2) + b * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float q0 = fminf(fmaxf(rintf(__fdiv_rn(v[2 * j], scale)), -8.0f), 7.0f);
+            const float q1 = fminf(fmaxf(rintf(__fdiv_rn(v[2 * j + 1], scale)), -8.0f), 7.0f);
+            dst[j] = (uint8_t)((((int)q1 & 0xF) << 4) | ((int)q0 & 0xF));
+        }
+    }
+}
+
+cudaError_t launch_synth_f16(void* out, uint64_t n, uint64_t seed, uint64_t stream, float amp, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    uint64_t g = (n + 255) / 256;
+    if (g > 148 * 64) g = 148 * 64;
+    k_synth_f16<<<(unsigned)g, 256, 0, s>>>(static_cast<__half*>(out), n, seed, stream, amp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_int4(void* out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream, float amp,
+                              cudaStream_t s) {
+    const uint64_t n = (uint64_t)N * (K / 32);
+    if (!n) return cudaSuccess;
+    uint64_t g = (n + 127) / 128;
+    if (g > 148 * 64) g = 148 * 64;
+    k_synth_int4<<<(unsigned)g, 128, 0, s>>>(static_cast<uint8_t*>(out), N, K, seed, stream, amp);
+    return cudaGetLastError();
+}
+
+}  // namespace lssm

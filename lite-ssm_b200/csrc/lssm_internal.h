@@ -1,0 +1,105 @@
+// lssm_internal.h — host-side plumbing shared by the C-ABI translation units:
+// the context object, thread-local error reporting, status macros and the
+// launcher declarations each kernel file exports to the C-ABI layer.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "lssm_cuda.h"
+
+struct lssm_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool owns_stream = false;
+    bool batch_active = false;
+    int sm_count = 148;
+    // Device-side error word for bounded waits inside kernels (0 = ok).
+    int* d_error = nullptr;
+};
+
+namespace lssm {
+
+void set_error(const char* fmt, ...);
+lssm_status fail(lssm_status st, const char* fmt, ...);
+lssm_status cuda_fail(cudaError_t e, const char* what);
+
+// Called after every op launch: checks the launch, and outside a batch waits for
+// completion (the one-shot semantics of src/backend/metal/ops.mm:131-148).
+lssm_status finish_op(lssm_ctx* ctx, const char* name);
+
+inline const uint8_t* bp(const void* p, size_t off) { return static_cast<const uint8_t*>(p) + off; }
+inline uint8_t* bp(void* p, size_t off) { return static_cast<uint8_t*>(p) + off; }
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---- launchers (kernel files) ------------------------------------------------
+// All take device pointers that already include byte offsets; they enqueue on `s`
+// and return cudaGetLastError().
+cudaError_t launch_rmsnorm_f16(const void* x, const void* w, void* y, uint32_t rows, uint32_t dim, float eps,
+                               cudaStream_t s);
+cudaError_t launch_silu_f16(const void* x, void* y, uint32_t n, cudaStream_t s);
+cudaError_t launch_add_inplace_f16(void* y, const void* x, uint32_t n, cudaStream_t s);
+cudaError_t launch_silu_gated_f16(const void* z, const void* g, void* y, uint32_t n, cudaStream_t s);
+cudaError_t launch_split_silu_xBC_f16(const void* xBC, void* xo, void* Bo, void* Co, uint32_t L, uint32_t d_inner,
+                                      uint32_t d_state, uint32_t n_groups, cudaStream_t s);
+cudaError_t launch_causal_conv1d_f16(const void* x, const void* w, const void* bias, void* y, uint32_t B,
+                                     uint32_t L, uint32_t D, uint32_t K, cudaStream_t s);
+cudaError_t launch_causal_conv1d_update_f16(const void* x_new, void* state, const void* w, const void* bias,
+                                            void* y, uint32_t B, uint32_t D, uint32_t K, cudaStream_t s);
+cudaError_t launch_seed_conv_state_f16(const void* xBC, void* state, uint32_t L, uint32_t D, uint32_t K,
+                                       cudaStream_t s);
+// Batched variant used by the engine: xBC (B, L, D) -> state (B, D, K).
+cudaError_t launch_seed_conv_state_batched(const void* xBC, void* state, uint32_t B, uint32_t L, uint32_t D,
+                                           uint32_t K, cudaStream_t s);
+
+// GEMV family (M <= 8 activation rows). epilogue: 0 store, 1 silu.
+cudaError_t launch_gemv_f16(const void* x, const void* w, void* y, uint32_t M, uint32_t N, uint32_t K,
+                            const void* norm_w, float eps, int epilogue, cudaStream_t s);
+cudaError_t launch_gemv_int4(const void* x, const void* packed, const void* scales, void* y, uint32_t M,
+                             uint32_t N, uint32_t K, cudaStream_t s);
+
+// GEMM (M rows of activations). Y[M,N] = X[M,K] W[N,K]^T; epilogue 0 store, 1 silu.
+cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, uint32_t N, uint32_t K,
+                            int epilogue, cudaStream_t s);
+// INT4 weights dequantised (rounded to fp16, like shaders/linear.metal:538) into
+// `scratch` (N*K halves, caller-owned) and multiplied with the fp16 GEMM.
+cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void* out, uint32_t N, uint32_t K,
+                                    cudaStream_t s);
+
+cudaError_t launch_ssd_step(const void* x, const void* B, const void* C, const void* dt_raw, const void* dt_bias,
+                            const void* A_log, const void* D, float* state, void* y, uint32_t batch, uint32_t H,
+                            uint32_t P, uint32_t N, uint32_t G, float dt_min, float dt_max, uint32_t has_D,
+                            cudaStream_t s);
+
+struct SsdArgs {
+    const void* X; const void* B; const void* C; const void* dt_raw;
+    const void* dt_bias; const void* A_log; const void* D;
+    void* Y; float* state;
+    uint32_t batch, L, H, P, N, G, chunk;
+    float dt_min, dt_max;
+    uint32_t has_D;
+    uint32_t x_dtype, dt_dtype, param_dtype, y_dtype;
+    // Element strides (in elements) for X/Y rows, B/C rows and dt rows; 0 = dense default.
+    uint64_t x_row_stride, bc_row_stride, dt_row_stride, y_row_stride;
+};
+cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s);
+
+// ssd_step over `batch` sequences with per-sequence strides (elements). When z is set
+// the output is the gated value half(silu(z) * half(y)) instead of y.
+struct StepArgs {
+    const __half* x; const __half* B; const __half* C; const __half* dt_raw;
+    const __half* dt_bias; const __half* A_log; const __half* D;
+    float* state; __half* y; const __half* z;
+    uint32_t batch, H, P, N, G;
+    float dt_min, dt_max;
+    uint32_t has_D;
+    uint64_t x_bs, bc_bs, dt_bs, y_bs, z_bs;
+};
+cudaError_t launch_ssd_step_ex(const StepArgs& a, cudaStream_t s);
+
+}  // namespace lssm

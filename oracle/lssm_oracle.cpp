@@ -888,6 +888,51 @@ int lssm_oracle_generate(const uint8_t* base, const OracleModelDesc* mdp, const 
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+//  Seeded synthetic weights on the CPU: the same recipe as the GPU generator
+//  (lite-ssm_b200/csrc/synth_rng.h), so the CPU baseline and the parity tests can
+//  build a bit-identical copy of a synthesized model without a GPU.
+//  f16: out[i] = half(value(seed, stream, i, amp)).
+//  int4: values rounded to fp16, then the block-32 quantiser above.
+// ---------------------------------------------------------------------------
+}  // extern "C"
+#include "../lite-ssm_b200/csrc/synth_rng.h"
+extern "C" {
+
+void lssm_oracle_synth_f32(float* out, uint64_t n, uint64_t seed, uint64_t stream, float amp) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = synth_value(seed, stream, i, amp);
+}
+
+void lssm_oracle_synth_f16(uint16_t* out, uint64_t n, uint64_t seed, uint64_t stream, float amp) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; ++i) out[i] = f2h(synth_value(seed, stream, (uint64_t)i, amp));
+}
+
+void lssm_oracle_synth_int4(uint8_t* out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream, float amp) {
+    uint16_t* scales = reinterpret_cast<uint16_t*>(out + (size_t)N * K / 2);
+    const uint32_t nb = K / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < (int64_t)N; ++n) {
+        float v[32];
+        for (uint32_t b = 0; b < nb; ++b) {
+            float absmax = 0.0f;
+            for (int j = 0; j < 32; ++j) {
+                v[j] = hr(synth_value(seed, stream, (uint64_t)n * K + b * 32 + j, amp));
+                absmax = std::max(absmax, std::fabs(v[j]));
+            }
+            absmax = std::max(absmax, 1e-12f);
+            const float scale = absmax / 7.0f;
+            scales[(size_t)n * nb + b] = f2h(scale);
+            uint8_t* dst = out + (size_t)n * (K / 2) + (size_t)b * 16;
+            for (int j = 0; j < 16; ++j) {
+                const float q0 = std::min(std::max(std::nearbyint(v[2 * j] / scale), -8.0f), 7.0f);
+                const float q1 = std::min(std::max(std::nearbyint(v[2 * j + 1] / scale), -8.0f), 7.0f);
+                dst[j] = (uint8_t)((((int)q1 & 0xF) << 4) | ((int)q0 & 0xF));
+            }
+        }
+    }
+}
+
 uint32_t lssm_oracle_sizeof_layer_offsets(void) { return (uint32_t)sizeof(OracleLayerOffsets); }
 uint32_t lssm_oracle_sizeof_model_desc(void) { return (uint32_t)sizeof(OracleModelDesc); }
 

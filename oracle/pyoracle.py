@@ -204,6 +204,104 @@ class OracleModel:
         return toks, pl, sl
 
 
+def mamba2_tensor_list(hp: dict, int4: bool):
+    """(name, dtype, shape) of a Mamba2ForCausalLM state_dict in its order — the order
+    the reference exporter writes (tools/export_mamba2.py:162-195); in_proj/out_proj
+    are INT4_B32 when int4 (export_mamba2.py:55-65)."""
+    dm, di = hp["d_model"], hp["expand"] * hp["d_model"]
+    G = hp.get("n_groups", 1) or 1
+    xd = di + 2 * G * hp["d_state"]
+    proj = di + xd + hp["n_heads"]
+    lin = DTYPE_INT4_B32 if int4 else DTYPE_F16
+    out = [("backbone.embeddings.weight", DTYPE_F16, (hp["vocab_size"], dm))]
+    for i in range(hp["n_layer"]):
+        p = f"backbone.layers.{i}."
+        out += [(p + "norm.weight", DTYPE_F16, (dm,)), (p + "mixer.dt_bias", DTYPE_F16, (hp["n_heads"],)),
+                (p + "mixer.A_log", DTYPE_F16, (hp["n_heads"],)), (p + "mixer.D", DTYPE_F16, (hp["n_heads"],)),
+                (p + "mixer.conv1d.weight", DTYPE_F16, (xd, 1, hp["d_conv"])),
+                (p + "mixer.conv1d.bias", DTYPE_F16, (xd,)),
+                (p + "mixer.in_proj.weight", lin if dm % 32 == 0 else DTYPE_F16, (proj, dm)),
+                (p + "mixer.norm.weight", DTYPE_F16, (di,)),
+                (p + "mixer.out_proj.weight", lin if di % 32 == 0 else DTYPE_F16, (dm, di))]
+    out += [("backbone.norm_f.weight", DTYPE_F16, (dm,)), ("lm_head.weight", DTYPE_F16, (hp["vocab_size"], dm))]
+    return out
+
+
+def plan_layout(hp: dict, tensors):
+    """Header + index bytes and payload offsets, restating tools/ssm_format.py:197-340."""
+    idx_size = sum(_align(32 + 8 * len(s) + len(n.encode()), 8) for n, _, s in tensors)
+    data_off = _align(HEADER_SIZE + idx_size, 64)
+    cur, placed = data_off, []
+    for n, dt, s in tensors:
+        nb = packed_nbytes(dt, int(np.prod(s)))
+        placed.append(TensorInfo(n, dt, tuple(s), cur, nb))
+        cur = _align(cur + nb, 64)
+    header = struct.pack(HEADER_FMT, b"LSSM", 1, HEADER_SIZE, len(tensors), HEADER_SIZE, data_off, hp["d_model"],
+                         hp["n_layer"], hp["d_state"], hp["d_conv"], hp["expand"], hp["vocab_size"], hp["n_heads"],
+                         hp["d_head"], hp.get("chunk_size", 256), DTYPE_F16, hp.get("n_groups", 1) or 1,
+                         hp.get("norm_before_gate", 0), 0, 0, 0, 0)
+    index = b""
+    for t in placed:
+        body = struct.pack(INDEX_PREFIX_FMT, len(t.name.encode()), len(t.shape), t.dtype, 0, t.offset, t.nbytes)
+        body += struct.pack(f"<{len(t.shape)}Q", *t.shape) + t.name.encode()
+        index += body + b"\0" * (_align(len(body), 8) - len(body))
+    return header + index, placed, _align(cur, 64)
+
+
+def _host_vector(kind: str, seed: int, stream: int, n: int) -> np.ndarray:
+    import math
+    lib().lssm_oracle_synth_f32.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float]
+    u = np.zeros(n, dtype=np.float32)
+    lib().lssm_oracle_synth_f32(ptr(u), n, seed, stream, 1.0)
+    out = np.zeros(n, dtype=np.float16)
+    for i in range(n):
+        uu = 0.5 * (float(u[i]) + 1.0)
+        if kind == "A_log":
+            v = math.log(1.0 + 15.0 * uu)
+        elif kind == "dt_bias":
+            dt = math.exp(math.log(1e-3) + uu * math.log(100.0))
+            v = dt + math.log(-math.expm1(-dt))
+        elif kind == "D":
+            v = 0.5 + uu
+        else:
+            v = 0.9 + 0.2 * uu
+        out[i] = np.float16(np.float32(v))
+    return out
+
+
+def synthesize(hp: dict, seed: int, int4: bool) -> bytes:
+    """CPU copy of the engine's seeded random-init model (.ssm image bytes)."""
+    L = lib()
+    L.lssm_oracle_synth_f16.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float]
+    L.lssm_oracle_synth_int4.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint64, C.c_float]
+    tl = mamba2_tensor_list(hp, int4)
+    head, placed, total = plan_layout(hp, tl)
+    img = np.zeros(total, dtype=np.uint8)
+    img[: len(head)] = np.frombuffer(head, dtype=np.uint8)
+    sqrt3 = 1.7320508075688772
+    for i, t in enumerate(placed):
+        stream = i + 1
+        view = img[t.offset: t.offset + t.nbytes]
+        addr = view.ctypes.data_as(C.c_void_p)
+        n = t.name
+        if n.endswith("embeddings.weight") or n == "lm_head.weight":
+            L.lssm_oracle_synth_f16(addr, int(np.prod(t.shape)), seed, 1 if n == "lm_head.weight" else stream,
+                                    float(np.float32(0.5 * sqrt3)))
+        elif n.endswith("in_proj.weight") or n.endswith("out_proj.weight"):
+            amp = float(np.float32(sqrt3 / np.sqrt(float(t.shape[1]))))
+            if t.dtype == DTYPE_INT4_B32:
+                L.lssm_oracle_synth_int4(addr, t.shape[0], t.shape[1], seed, stream, amp)
+            else:
+                L.lssm_oracle_synth_f16(addr, int(np.prod(t.shape)), seed, stream, amp)
+        elif n.endswith("conv1d.weight") or n.endswith("conv1d.bias"):
+            L.lssm_oracle_synth_f16(addr, int(np.prod(t.shape)), seed, stream, 0.5)
+        else:
+            kind = "A_log" if n.endswith("A_log") else "dt_bias" if n.endswith("dt_bias") else \
+                "D" if n.endswith(".D") else "norm"
+            view[:] = np.frombuffer(_host_vector(kind, seed, stream, int(np.prod(t.shape))).tobytes(), np.uint8)
+    return img.tobytes()
+
+
 def f16(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.float32).astype(np.float16).view(np.uint16))
 
