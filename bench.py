@@ -1,0 +1,375 @@
+"""Benchmark of the B200 Mamba-2 hot path (the BASELINE metric: 2.7B-shape INT4
+decode / prefill tokens per second, with roofline fractions).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode27b|ssd|batched]
+
+Default workload (N=1): the Mamba-2 2.7B shape (64 layers, d_model 2560, d_inner 5120,
+80 heads x 64, d_state 128, ngroups 1, vocab 50288), in_proj/out_proj packed INT4_B32 as
+the reference exporter writes them, random init from seed 0; one step = one request:
+prefill 2048 random prompt ids + 512 greedy decode tokens, batch 1. `value` is decode
+tokens/s (whole job), `prefill_tok_s` the prefill rate. Under torchrun each rank serves
+its own independent request (sequences sharded across GPUs, no data-path collective):
+weak scaling. Timing: W untimed steps, then K steps bracketed by a barrier and a device
+synchronize; prefill and decode are timed with CUDA events on the engine's stream; the
+max over ranks is reported. `e2e` repeats the request through the C ABI call with the
+prompt in pinned host memory and the generated ids copied back, timed on the host.
+
+--impl reference times the reference's math on the host CPU (the reference has no CPU
+compute path of its own: its kernels are Metal shaders; the oracle under oracle/ is the
+C++ restatement of them) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "lite-ssm_b200"))
+
+METRIC = "decode tok/s & prefill tok/s (2.7B quant) at 1/2/4/8 B200; % HBM/tensor roofline"
+HP27 = dict(d_model=2560, n_layer=64, d_state=128, d_conv=4, expand=2, vocab_size=50288, n_heads=80, d_head=64,
+            chunk_size=256, n_groups=1, norm_before_gate=0)
+PROMPT, NEW = 2048, 512
+VOCAB_IDS = 50280
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(j.get("bf16_tflops_sustained", 0)), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def decode_bytes_per_token(hp) -> dict:
+    """Algorithmic HBM bytes of one batch-1 decode token (each byte read/written once)."""
+    dm, di, H, P, N = hp["d_model"], hp["expand"] * hp["d_model"], hp["n_heads"], hp["d_head"], hp["d_state"]
+    G = hp["n_groups"]
+    xd = di + 2 * G * N
+    proj = di + xd + H
+    int4 = lambda n, k: n * k // 2 + (n * k // 32) * 2  # noqa: E731
+    per_layer = {
+        "in_proj_int4": int4(proj, dm),
+        "out_proj_int4": int4(dm, di),
+        "ssd_state_rw": 2 * H * P * N * 4,
+        "conv_state_rw": 2 * xd * hp["d_conv"] * 2,
+        "small": (xd * hp["d_conv"] + xd + 3 * H + dm + di) * 2,
+    }
+    layers = hp["n_layer"] * sum(per_layer.values())
+    lm = hp["vocab_size"] * dm * 2 + dm * 2
+    return dict(per_layer=per_layer, total=layers + lm, lm_head=lm)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local, dist
+
+
+def barrier(dist, local):
+    if dist is not None:
+        import torch
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+
+def allreduce_max(dist, vals, local):
+    if dist is None:
+        return vals
+    import torch
+    t = torch.tensor(vals, dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=200):
+    """Average device time of the dominant decode kernel (the in_proj INT4 GEMV,
+    N = 10576, K = 2560) on layer 0's weights, CUDA events on the launching stream."""
+    import ctypes as C
+
+    import torch
+    dm = hp["d_model"]
+    off, nb, _ = model.tensor("backbone.layers.0.mixer.in_proj.weight")
+    N = (2 * hp["expand"] * dm + 2 * hp["n_groups"] * hp["d_state"] + hp["n_heads"])
+    base = lssm.lib().lssm_model_device_base(model.h)
+    x = lssm.DeviceBuffer(ctx, dm * 2)
+    x.upload(np.random.default_rng(0).standard_normal(dm).astype(np.float16))
+    y = lssm.DeviceBuffer(ctx, N * 2)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    dims = lssm.LinearDims(1, N, dm)
+    L = lssm.lib()
+
+    class _B:
+        pass
+
+    def call():
+        lssm.check(L.lssm_linear_int4_gemv(ctx.h, x.ptr, 0, base, off, base, off + N * dm // 2, y.ptr, 0, dims))
+
+    ctx.begin_batch()
+    for _ in range(10):
+        call()
+    ctx.commit_and_wait()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.begin_batch()
+    e0.record(stream)
+    for _ in range(reps):
+        call()
+    e1.record(stream)
+    ctx.commit_and_wait()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    bytes_alg = nb + dm * 2 + N * 2
+    _ = C
+    return ms, bytes_alg
+
+
+def cpu_baseline_sample(seed=0, prompt=32, new=8, hp=None):
+    """The oracle (C++ restatement of the reference's kernels) on the host cores:
+    a bounded sample of the same workload (same model bytes, shorter request)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle as po
+    hp = hp or HP27
+    t0 = time.time()
+    img = po.synthesize(hp, seed, True)
+    t_synth = time.time() - t0
+    m = po.OracleModel(img, mode=0)
+    del img
+    rng = np.random.default_rng(seed + 1)
+    toks = rng.integers(0, VOCAB_IDS, size=prompt).astype(np.uint32)
+    # prefill alone
+    t0 = time.time()
+    m.generate(toks, 1, want_logits=False)
+    t_pre = time.time() - t0
+    t0 = time.time()
+    m.generate(toks, new + 1, want_logits=False)
+    t_all = time.time() - t0
+    t_dec = max(t_all - t_pre, 1e-9)
+    return dict(prefill_tok_s=prompt / t_pre, decode_tok_s=new / t_dec, cores=po.lib().lssm_oracle_num_threads(),
+                sample=f"prompt {prompt} + {new} greedy tokens, full 64-layer 2.7B INT4 model (synth {t_synth:.1f}s)",
+                seconds=t_pre + t_all)
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    res = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline_sample(prompt=args.ref_prompt, new=args.ref_new)
+        if i >= args.warmup:
+            res.append(r)
+    dec = float(np.median([r["decode_tok_s"] for r in res]))
+    pre = float(np.median([r["prefill_tok_s"] for r in res]))
+    secs = float(np.mean([r["seconds"] for r in res]))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": dec, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 activations, int4_b32 weights, f32 accum",
+        "data": "synthetic (seeded random-init weights and prompt ids)",
+        "config": {"workload": "2.7B-int4 batch-1 decode (CPU bounded sample)", "model": "mamba2-2.7b-shape",
+                   "global_batch": 1, "seq_len": args.ref_prompt, "parallelism": "host threads"},
+        "prefill_tok_s": pre,
+        "cpu_baseline": {"value": dec, "unit": "tok/s", "cores": res[0]["cores"], "kind": "port",
+                         "sample": res[0]["sample"]},
+        "e2e": {"value": dec, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local, dist):
+    import lssm
+    import torch
+    hbm, tflops, tflops_sus, peak_kind = measured_peaks()
+    ctx = lssm.Ctx(local)
+    hp = lssm.hparams(**HP27)
+    model = lssm.Model.synthesize(ctx, hp, seed=0, int4=True)
+    sess = lssm.Session(ctx, model, batch=1, max_seq_len=PROMPT)
+    rng = np.random.default_rng(1000 + rank)
+    prompt = rng.integers(0, VOCAB_IDS, size=(1, PROMPT)).astype(np.uint32)
+
+    def step():
+        sess.reset()
+        first = sess.prefill(prompt)
+        p_ms, _ = sess.timing()
+        sess.decode(first, NEW - 1)   # NEW tokens total: 1 from prefill + NEW-1 decode steps
+        _, d_ms = sess.timing()
+        return p_ms, d_ms
+
+    for _ in range(args.warmup):
+        step()
+    barrier(dist, local)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    pre_ms, dec_ms = [], []
+    w0 = time.time()
+    for _ in range(args.steps):
+        p, d = step()
+        pre_ms.append(p)
+        dec_ms.append(d)
+    torch.cuda.synchronize()
+    wall = time.time() - w0
+    barrier(dist, local)
+    clk = clocks.stop()
+    tot_pre, tot_dec = allreduce_max(dist, [sum(pre_ms), sum(dec_ms)], local)
+    dec_tokens = (NEW - 1) * args.steps * world
+    pre_tokens = PROMPT * args.steps * world
+    decode_tok_s = dec_tokens / (tot_dec / 1000.0)
+    prefill_tok_s = pre_tokens / (tot_pre / 1000.0)
+
+    # e2e through the C ABI with host buffers (prompt H2D + generated ids D2H in the timed region)
+    pinned = torch.from_numpy(prompt).pin_memory()
+    ptoks = pinned.numpy()
+    barrier(dist, local)
+    e_t = []
+    for _ in range(max(1, min(args.steps, 3))):
+        t0 = time.perf_counter()
+        out = sess.generate(ptoks, NEW)
+        e_t.append(time.perf_counter() - t0)
+    (e_max,) = allreduce_max(dist, [float(np.sum(e_t))], local)
+    e2e = (NEW - 1) * len(e_t) * world / e_max
+    assert out.shape == (1, NEW)
+
+    # dominant-kernel roofline (INT4 GEMV, measured live)
+    k_ms, k_bytes = time_kernel_int4_gemv(lssm, ctx, model, HP27)
+    achieved = k_bytes / (k_ms / 1000.0) / 1e9
+    bpt = decode_bytes_per_token(HP27)
+    step_gbs = bpt["total"] * (decode_tok_s / world) / 1e9
+    prof = ROOT / "profiles" / "int4_gemv_inproj_traffic.json"
+    traffic = json.loads(prof.read_text()).get("traffic_bytes_per_launch") if prof.exists() else None
+    n_pre, n_dec = sess.launches()
+    launches = args.steps * (n_pre + (NEW - 1) * n_dec)
+    prefill_flops = 2 * PROMPT * (HP27["n_layer"] * ((2 * 5120 + 256 + 80) * 2560 + 2560 * 5120))
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": (tot_pre + tot_dec) / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 activations, int4_b32 weights, f32 accum",
+            "data": "synthetic (seeded random-init weights in the reference .ssm INT4_B32 layout, random prompt ids)",
+            "config": {"workload": "2.7B-int4 batch-1 per GPU: prefill 2048 + 512 greedy decode tokens",
+                       "model": "mamba2-2.7b-shape (64L, d_model 2560, 80x64 heads, d_state 128, vocab 50288)",
+                       "global_batch": world, "seq_len": PROMPT, "parallelism": f"independent sequences x{world}",
+                       "l2": "no flush: each decode token streams 2.05 GB of weights + state (> 126 MB L2)"},
+            "prefill_tok_s": prefill_tok_s,
+            "decode_ms_per_token": tot_dec / ((NEW - 1) * args.steps),
+            "prefill_ms": tot_pre / args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": traffic, "kernel": "int4 GEMV in_proj (N=10576, K=2560)",
+                         "kernel_ms": k_ms, "bytes_per_launch": k_bytes, "peak_kind": f"{peak_kind} hbm_gbs"},
+            "decode_step_roofline": {"bytes_per_token": bpt["total"], "achieved_gbs": step_gbs, "peak": hbm,
+                                     "frac": step_gbs / hbm},
+            "prefill_tensor_roofline": {"flops": prefill_flops,
+                                        "achieved_tflops": prefill_flops / (tot_pre / args.steps / 1000) / 1e12,
+                                        "peak": tflops, "frac": prefill_flops / (tot_pre / args.steps / 1000) / 1e12 / tflops},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": NEW * 4},
+            "gpu_launches": launches, "clocks": clk, "wall_s": wall,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_baseline_sample(prompt=args.ref_prompt, new=args.ref_new)
+            line["cpu_baseline"] = {"value": cb["decode_tok_s"], "unit": "tok/s", "cores": cb["cores"], "kind": "port",
+                                    "sample": cb["sample"], "prefill_tok_s": cb["prefill_tok_s"]}
+        print(json.dumps(line), flush=True)
+    sess.close()
+    model.close()
+    ctx.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-prompt", type=int, default=32)
+    ap.add_argument("--ref-new", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
+    world, rank, local, dist = dist_setup(args.gpus)
+    try:
+        return run_ours(args, world, rank, local, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

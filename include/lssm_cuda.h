@@ -226,6 +226,8 @@ lssm_status lssm_generate(lssm_session* s, const uint32_t* prompt, uint32_t L, u
 lssm_status lssm_session_logits(lssm_session* s, float* out);
 /* Device timing of the last prefill / decode call (CUDA events on the session stream), ms. */
 lssm_status lssm_session_timing(lssm_session* s, float* prefill_ms, float* decode_ms);
+/* Kernel launches issued by the last prefill and by one decode step. */
+lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* decode_step);
 /* Engine knobs: "cuda_graph" 1 = capture each decode step in a CUDA graph (default 1). */
 lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t value);
 

@@ -491,6 +491,8 @@ struct lssm_session {
     int* d_err = nullptr;
     cudaEvent_t ev[4] = {};
     float prefill_ms = 0.0f, decode_ms = 0.0f;
+    uint64_t nl = 0;                          // kernel launches issued (running count)
+    uint64_t prefill_launches = 0, decode_step_launches = 0;
     bool use_graph = true;
     cudaGraphExec_t graph = nullptr;
     bool logits_valid = false;
@@ -615,23 +617,28 @@ static lssm_status linear(lssm_session* s, const TensorRec* w, const __half* x, 
                                    epilogue, st));
         else
             CU(launch_gemv_f16(x, wp, y, rows, N, K, nw, 1e-5f, epilogue, st));
+        s->nl += 1;
         return LSSM_OK;
     }
     const __half* xin = x;
     if (prenorm) {
         CU(launch_rmsnorm_f16(x, W(m, prenorm), s->normed, rows, K, 1e-5f, st));
+        s->nl += 1;
         xin = s->normed;
     }
     const void* wf = wp;
     if (w->dtype == DT_INT4_B32) {
         CU(launch_int4_dequant_f16(wp, static_cast<const uint8_t*>(wp) + (size_t)N * K / 2, s->wscratch, N, K, st));
+        s->nl += 1;
         wf = s->wscratch;
     }
     if (epilogue == 2) {
         CU(launch_gemm_f16(xin, wf, s->bout, rows, N, K, 0, st));
         CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
+        s->nl += 2;
     } else {
         CU(launch_gemm_f16(xin, wf, y, rows, N, K, epilogue, st));
+        s->nl += 1;
     }
     return LSSM_OK;
 }
@@ -666,6 +673,7 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
         a.x_bs = di; a.bc_bs = GN; a.dt_bs = proj; a.y_bs = di; a.z_bs = proj;
         CU(launch_ssd_step_ex(a, st));
+        s->nl += 2;
     } else {
         CU(launch_conv_silu_split(xbc, proj, W(m, lw.conv_w), W(m, lw.conv_b), s->xs, s->Bs, s->Cs, B, L, di, GN, Kc, st));
         SsdArgs a{};
@@ -678,11 +686,15 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         a.x_row_stride = di; a.bc_row_stride = GN; a.dt_row_stride = proj; a.y_row_stride = di;
         CU(launch_ssd_chunked(a, st));
         CU(launch_gate(zc, proj, s->ys, s->gated, rows, di, st));
+        s->nl += 3;
     }
     // 7+8+9. gated RMSNorm + out_proj + residual add into hidden
     if ((r = linear(s, lw.out_proj, s->gated, s->hidden, rows, dm, di, lw.mixer_norm, 2, st))) return r;
     // 10. seed conv state from pre-conv xBC after a prefill
-    if (!decode) CU(launch_seed_strided(xbc, proj, conv, B, L, xd, Kc, st));
+    if (!decode) {
+        CU(launch_seed_strided(xbc, proj, conv, B, L, xd, Kc, st));
+        s->nl += 1;
+    }
     return LSSM_OK;
 }
 
@@ -726,9 +738,11 @@ extern "C" lssm_status lssm_prefill(lssm_session* s, const uint32_t* tokens, uin
     lssm_model* m = s->m;
     const SsmHeader& h = m->img.hdr;
     const uint32_t rows = s->batch * L;
-    CU(cudaEventRecord(s->ev[0], st));
     CU(cudaMemcpyAsync(s->d_tokens, tokens, (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+    const uint64_t nl0 = s->nl;
+    CU(cudaEventRecord(s->ev[0], st));   // device timing starts with the tokens resident in HBM
     CU(launch_embed_gather(s->d_tokens, W(m, m->embed), s->hidden, rows, h.d_model, h.vocab_size, s->d_err, st));
+    s->nl += 1;
     for (uint32_t l = 0; l < h.n_layer; ++l)
         if (lssm_status r = run_block(s, l, L, false, st)) return r;
     // last row of each sequence -> contiguous (batch, d_model)
@@ -736,6 +750,8 @@ extern "C" lssm_status lssm_prefill(lssm_session* s, const uint32_t* tokens, uin
                          (size_t)L * h.d_model * 2, (size_t)h.d_model * 2, s->batch, cudaMemcpyDeviceToDevice, st));
     if (lssm_status r = logits_of(s, s->lastrows, st)) return r;
     CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, nullptr, 0, nullptr, nullptr, nullptr, 0, st));
+    s->nl += 1;
+    s->prefill_launches = s->nl - nl0;
     CU(cudaEventRecord(s->ev[1], st));
     if (next_tokens) CU(cudaMemcpyAsync(next_tokens, s->d_cur, (size_t)s->batch * 4, cudaMemcpyDeviceToHost, st));
     CU(cudaStreamSynchronize(st));
@@ -754,6 +770,7 @@ static lssm_status decode_step_body(lssm_session* s, cudaStream_t st) {
     if (lssm_status r = logits_of(s, s->hidden, st)) return r;
     CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, s->d_hist, s->hist_cap, s->d_step, W(m, m->embed),
                           s->hidden, h.d_model, st));
+    s->nl += 2;
     return LSSM_OK;
 }
 
@@ -777,7 +794,9 @@ extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint3
     if (s->use_graph && !s->graph) {
         cudaGraph_t g;
         CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        const uint64_t nl0 = s->nl;
         lssm_status r = decode_step_body(s, st);
+        s->decode_step_launches = s->nl - nl0;
         cudaError_t e = cudaStreamEndCapture(st, &g);
         if (r) { if (e == cudaSuccess) cudaGraphDestroy(g); return r; }
         if (e != cudaSuccess) return cuda_fail(e, "decode graph capture");
@@ -788,7 +807,11 @@ extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint3
     CU(cudaEventRecord(s->ev[2], st));
     for (uint32_t i = 0; i < n_steps; ++i) {
         if (s->graph) CU(cudaGraphLaunch(s->graph, st));
-        else if (lssm_status r = decode_step_body(s, st)) return r;
+        else {
+            const uint64_t nl0 = s->nl;
+            if (lssm_status r = decode_step_body(s, st)) return r;
+            s->decode_step_launches = s->nl - nl0;
+        }
     }
     CU(cudaEventRecord(s->ev[3], st));
     if (out_tokens) {
@@ -836,6 +859,13 @@ extern "C" lssm_status lssm_session_logits(lssm_session* s, float* out) {
         __half hv = *reinterpret_cast<__half*>(&tmp[i]);
         out[i] = __half2float(hv);
     }
+    return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* decode_step) {
+    if (!s) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_launches: null session");
+    if (prefill) *prefill = s->prefill_launches;
+    if (decode_step) *decode_step = s->decode_step_launches;
     return LSSM_OK;
 }
 

@@ -117,6 +117,7 @@ _SIGS = {
     "lssm_session_logits": [P, P],
     "lssm_session_timing": [P, C.POINTER(f32), C.POINTER(f32)],
     "lssm_session_set_option": [P, C.c_char_p, C.c_int64],
+    "lssm_session_launches": [P, C.POINTER(u64), C.POINTER(u64)],
 }
 _OTHER = {
     "lssm_last_error": (C.c_char_p, []),
@@ -443,6 +444,11 @@ class Session:
     def timing(self):
         a, b = f32(), f32()
         check(lib().lssm_session_timing(self.h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def launches(self):
+        a, b = u64(), u64()
+        check(lib().lssm_session_launches(self.h, C.byref(a), C.byref(b)))
         return a.value, b.value
 
     def close(self):

@@ -35,12 +35,13 @@ def get16(buf, n, off=0):
 
 
 def ulp_close(a, b, ulps=1):
-    a16, b16 = np.float16(a), np.float16(b)
+    a16, b16 = np.float16(np.ravel(a)), np.float16(np.ravel(b))
     spacing = np.abs(np.spacing(np.maximum(np.abs(a16), np.abs(b16)).astype(np.float16))).astype(np.float32)
     return np.all(np.abs(a16.astype(np.float32) - b16.astype(np.float32)) <= ulps * spacing + 1e-7)
 
 
 def close(gpu, ref, rtol=1e-2, atol=1e-3):
+    gpu, ref = np.ravel(gpu), np.ravel(ref)
     err = np.abs(gpu - ref)
     ok = err <= atol + rtol * np.abs(ref)
     assert ok.all(), f"max err {err.max():.4g} at {np.argmax(err)}; ref {ref.ravel()[np.argmax(err)]:.4g}"
@@ -229,7 +230,7 @@ def test_conv1d_update(ctx, ops):
     bx, bs, bw, bb, by = hb(ctx, xn), hb(ctx, state), hb(ctx, w), hb(ctx, bias), lssm.DeviceBuffer(ctx, D * 2)
     for _ in range(1):
         ops.causal_conv1d_update_f16((bx, 0), (bs, 0), (bw, 0), (bb, 0), (by, 0), lssm.Conv1dDims(1, 1, D, K))
-    assert np.array_equal(bs.download(np.uint16, D * K), rs)
+    assert np.array_equal(bs.download(np.uint16, D * K), rs.ravel())
     close(get16(by, D), po.to_f32(ry), rtol=2e-3, atol=2e-3)
 
 
