@@ -298,7 +298,7 @@ def run_ours(args, world, rank, local, dist):
         out = sess.generate(ptoks, NEW)
         e_t.append(time.perf_counter() - t0)
     (e_max,) = allreduce_max(dist, [float(np.sum(e_t))], local)
-    e2e = (NEW - 1) * len(e_t) * world / e_max
+    e2e = NEW * len(e_t) * world / e_max   # generated tokens per request-second (prefill + decode + copies)
     assert out.shape == (1, NEW)
 
     # dominant-kernel roofline (INT4 GEMV, measured live)
@@ -356,7 +356,12 @@ def main():
     ap.add_argument("--ref-prompt", type=int, default=32)
     ap.add_argument("--ref-new", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt-len", type=int, default=PROMPT,
+                    help="prompt tokens per request (the metric's workload is 2048; smaller only for profiling)")
+    ap.add_argument("--decode-tokens", type=int, default=NEW,
+                    help="generated tokens per request (the metric's workload is 512; smaller only for profiling)")
     args = ap.parse_args()
+    globals()["PROMPT"], globals()["NEW"] = args.prompt_len, args.decode_tokens
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

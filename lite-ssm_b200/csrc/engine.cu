@@ -539,7 +539,9 @@ extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_
     SA(s->conv, s->conv_layer * h.n_layer * 2, "session: conv state");
     SA(s->ssd, s->ssd_layer * h.n_layer * 4, "session: ssd state");
     SA(s->hidden, rows * h.d_model * 2, "session: hidden");
-    SA(s->normed, rows * h.d_model * 2, "session: normed");
+    // normed holds the RMSNorm output of either linear's input (d_model for in_proj,
+    // d_inner for out_proj), so it is sized for the wider of the two.
+    SA(s->normed, rows * std::max<size_t>(h.d_model, m->d_inner) * 2, "session: normed");
     SA(s->proj, rows * m->proj * 2, "session: proj");
     SA(s->xs, rows * m->d_inner * 2, "session: x");
     SA(s->Bs, rows * m->GN * 2, "session: B");
