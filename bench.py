@@ -160,8 +160,11 @@ def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=200):
 
     import torch
     dm = hp["d_model"]
-    off, nb, _ = model.tensor("backbone.layers.0.mixer.in_proj.weight")
+    # every launch reads a different layer's in_proj (64 x 15 MB >> L2), as in a decode token
+    offs = [model.tensor(f"backbone.layers.{i}.mixer.in_proj.weight")[0] for i in range(hp["n_layer"])]
+    _, nb, _ = model.tensor("backbone.layers.0.mixer.in_proj.weight")
     N = (2 * hp["expand"] * dm + 2 * hp["n_groups"] * hp["d_state"] + hp["n_heads"])
+    calls = [0]
     base = lssm.lib().lssm_model_device_base(model.h)
     x = lssm.DeviceBuffer(ctx, dm * 2)
     x.upload(np.random.default_rng(0).standard_normal(dm).astype(np.float16))
@@ -174,6 +177,8 @@ def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=200):
         pass
 
     def call():
+        off = offs[calls[0] % len(offs)]
+        calls[0] += 1
         lssm.check(L.lssm_linear_int4_gemv(ctx.h, x.ptr, 0, base, off, base, off + N * dm // 2, y.ptr, 0, dims))
 
     ctx.begin_batch()
@@ -347,8 +352,147 @@ def run_ours(args, world, rank, local, dist):
     return 0
 
 
+def run_kernel_bench(args):
+    """Single-kernel microbenchmarks at the BASELINE shapes (used for the roofline
+    numbers and as small, bounded cases for ncu). Weights / states are cycled over
+    64 distinct layer slices so every launch reads from HBM (> 126 MB L2), like a
+    real decode token does."""
+    import ctypes as C
+
+    import lssm
+    import torch
+    hbm, tflops, _, peak_kind = measured_peaks()
+    ctx = lssm.Ctx(0)
+    L = lssm.lib()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    reps = args.reps
+    out = {"kernel": args.kernel}
+
+    def timed(call, n):
+        ctx.begin_batch()
+        for i in range(min(n, 8)):
+            call(i)
+        ctx.commit_and_wait()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.begin_batch()
+        e0.record(stream)
+        for i in range(n):
+            call(i)
+        e1.record(stream)
+        ctx.commit_and_wait()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    if args.kernel in ("int4_gemv", "int4_gemv_out"):
+        if args.kernel == "int4_gemv":
+            N, K = 10576, 2560
+        else:
+            N, K = 2560, 5120
+        per = N * K // 2 + N * K // 16
+        nl = 64
+        W = torch.randint(0, 256, (nl * per,), dtype=torch.uint8, device=dev, generator=g)
+        sc = (torch.rand((nl, N * K // 32), device=dev, generator=g) * 0.01 + 1e-3).half()
+        Wv = W.view(nl, per)
+        Wv[:, N * K // 2:] = sc.view(torch.uint8).view(nl, -1)
+        x = torch.randn(K, device=dev, generator=g).half()
+        y = torch.empty(N, device=dev, dtype=torch.half)
+        torch.cuda.synchronize()
+        dims = lssm.LinearDims(1, N, K)
+        base = W.data_ptr()
+
+        def call(i):
+            o = (i % nl) * per
+            lssm.check(L.lssm_linear_int4_gemv(ctx.h, x.data_ptr(), 0, base, o, base, o + N * K // 2, y.data_ptr(),
+                                               0, dims))
+        ms = timed(call, reps)
+        b = per + K * 2 + N * 2
+        out.update(shape=[N, K], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+    elif args.kernel in ("gemm_f16", "int4_gemm"):
+        M, N, K = args.m, args.n, args.k
+        X = torch.randn(M, K, device=dev, generator=g).half()
+        Y = torch.empty(M, N, device=dev, dtype=torch.half)
+        if args.kernel == "gemm_f16":
+            Wt = (torch.randn(N, K, device=dev, generator=g) / K ** 0.5).half()
+            torch.cuda.synchronize()
+
+            def call(i):
+                lssm.check(L.lssm_linear_f16_gemm(ctx.h, X.data_ptr(), 0, Wt.data_ptr(), 0, Y.data_ptr(), 0,
+                                                  lssm.LinearDims(M, N, K)))
+        else:
+            per = N * K // 2 + N * K // 16
+            Wq = torch.randint(0, 256, (per,), dtype=torch.uint8, device=dev, generator=g)
+            Wq[N * K // 2:] = (torch.rand(N * K // 32, device=dev, generator=g) * 0.01).half().view(torch.uint8)
+            torch.cuda.synchronize()
+
+            def call(i):
+                lssm.check(L.lssm_linear_int4_gemm(ctx.h, X.data_ptr(), 0, Wq.data_ptr(), 0, Wq.data_ptr(),
+                                                   N * K // 2, Y.data_ptr(), 0, lssm.LinearDims(M, N, K)))
+        ms = timed(call, reps)
+        fl = 2.0 * M * N * K
+        out.update(shape=[M, N, K], us=ms * 1e3, tflops=fl / ms / 1e9, frac=fl / ms / 1e9 / tflops)
+    elif args.kernel == "ssd_chunked":
+        Bt, Ls, H, P, N, G = args.ssd_batch, args.ssd_len, 80, 64, 128, 1
+        X = torch.randn(Bt, Ls, H, P, device=dev, generator=g).bfloat16()
+        Bm = torch.randn(Bt, Ls, G, N, device=dev, generator=g).bfloat16()
+        Cm = torch.randn(Bt, Ls, G, N, device=dev, generator=g).bfloat16()
+        dt = torch.randn(Bt, Ls, H, device=dev, generator=g) - 2.0
+        db = torch.zeros(H, device=dev)
+        alog = torch.empty(H, device=dev).uniform_(0.0, float(np.log(16.0)), generator=g)
+        Dd = torch.randn(H, device=dev, generator=g)
+        Y = torch.empty(Bt, Ls, H, P, device=dev)
+        S = torch.zeros(Bt, H, P, N, device=dev)
+        torch.cuda.synchronize()
+        dims = lssm.SSDBatchedDims(Bt, Ls, H, P, N, G, 256, 1e-6, 1e6, 1, lssm.DT_BF16, lssm.DT_F32, lssm.DT_F32,
+                                   lssm.DT_F32)
+
+        def call(i):
+            lssm.check(L.lssm_ssd_chunked_batched(ctx.h, X.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), dt.data_ptr(),
+                                                  db.data_ptr(), alog.data_ptr(), Dd.data_ptr(), Y.data_ptr(),
+                                                  S.data_ptr(), dims))
+        ms = timed(call, reps)
+        b = X.numel() * 2 + Bm.numel() * 2 * 2 + dt.numel() * 4 + Y.numel() * 4 + 2 * S.numel() * 4
+        out.update(shape=[Bt, Ls, H, P, N], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+    elif args.kernel == "ssd_step":
+        H, P, N, nl = 80, 64, 128, 64
+        S = torch.zeros(nl, H, P, N, device=dev)
+        x = torch.randn(H * P, device=dev, generator=g).half()
+        Bm = torch.randn(N, device=dev, generator=g).half()
+        Cm = torch.randn(N, device=dev, generator=g).half()
+        dt = torch.randn(H, device=dev, generator=g).half()
+        par = torch.zeros(H, device=dev).half()
+        y = torch.empty(H * P, device=dev, dtype=torch.half)
+        torch.cuda.synchronize()
+        dims = lssm.SSDStepDims(H, P, N, 1, 1e-6, 1e6, 1)
+
+        def call(i):
+            so = (i % nl) * H * P * N * 4
+            lssm.check(L.lssm_ssd_step_f16(ctx.h, x.data_ptr(), 0, Bm.data_ptr(), 0, Cm.data_ptr(), 0, dt.data_ptr(), 0,
+                                           par.data_ptr(), 0, par.data_ptr(), 0, par.data_ptr(), 0, S.data_ptr(), so,
+                                           y.data_ptr(), 0, dims))
+        ms = timed(call, reps)
+        b = 2 * H * P * N * 4 + H * P * 4
+        out.update(shape=[H, P, N], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+    out["peak"] = f"{peak_kind} (hbm {hbm} GB/s, bf16 {tflops} TF/s)"
+    print(json.dumps(out), flush=True)
+    _ = C
+    ctx.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default=None,
+                    choices=["int4_gemv", "int4_gemv_out", "gemm_f16", "int4_gemm", "ssd_chunked", "ssd_step"],
+                    help="single-kernel microbenchmark instead of the model bench")
+    ap.add_argument("--reps", type=int, default=64)
+    ap.add_argument("--m", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=10576)
+    ap.add_argument("--k", type=int, default=2560)
+    ap.add_argument("--ssd-batch", type=int, default=8)
+    ap.add_argument("--ssd-len", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -362,6 +506,8 @@ def main():
                     help="generated tokens per request (the metric's workload is 512; smaller only for profiling)")
     args = ap.parse_args()
     globals()["PROMPT"], globals()["NEW"] = args.prompt_len, args.decode_tokens
+    if args.kernel:
+        return run_kernel_bench(args)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
