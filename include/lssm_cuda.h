@@ -146,6 +146,22 @@ lssm_status lssm_inproj_fused_f16(lssm_ctx* ctx, const void* normed, size_t norm
                                   void* ssd_B, size_t b_off, void* ssd_C, size_t c_off, void* proj_dt,
                                   size_t dt_off, void* proj_xBC, size_t xBC_off,
                                   lssm_fused_inproj_dims dims);                         /* ops.hpp:203-214 */
+/* Same op and arguments as lssm_inproj_fused_f16, for callers that cannot allocate device
+ * memory at call time (a framework allocator that owns the whole memory budget, a serving
+ * loop where cudaMalloc/cudaFree would block or synchronise the device, a process that must
+ * not hit out-of-memory once running). It allocates nothing: its scratch (the fp32 matmul
+ * tile, L * proj_dim * 4 bytes) lives in a 4 MiB static device array that every GPU loading
+ * this library keeps until exit; larger requests return LSSM_ERR_INVALID_ARGUMENT. The array's
+ * device address is looked up on the first call on each device, so make that first call
+ * before any stream capture. All calls share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller. No counterpart in the reference (its in_proj kernel keeps
+ * the tile in threadgroup memory, shaders/fused.metal:71-76). */
+lssm_status lssm_inproj_fused_f16_noalloc(lssm_ctx* ctx, const void* normed, size_t normed_off, const void* W_in,
+                                          size_t w_in_off, const void* W_conv, size_t w_conv_off,
+                                          const void* conv_b, size_t conv_b_off, void* proj_z, size_t z_off,
+                                          void* ssd_x, size_t x_off, void* ssd_B, size_t b_off, void* ssd_C,
+                                          size_t c_off, void* proj_dt, size_t dt_off, void* proj_xBC,
+                                          size_t xBC_off, lssm_fused_inproj_dims dims);
 lssm_status lssm_ssd_chunked_f16(lssm_ctx* ctx, const void* X, size_t X_off, const void* B, size_t B_off,
                                  const void* C, size_t C_off, const void* dt_raw, size_t dt_off,
                                  const void* dt_bias, size_t db_off, const void* A_log, size_t A_off,

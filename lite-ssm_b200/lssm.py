@@ -98,6 +98,7 @@ _SIGS = {
     "lssm_causal_conv1d_update_f16": [P, P, sz, P, sz, P, sz, P, sz, P, sz, Conv1dDims],
     "lssm_seed_conv_state_f16": [P, P, sz, P, sz, u32, u32, u32],
     "lssm_inproj_fused_f16": [P] + [P, sz] * 10 + [FusedInProjDims],
+    "lssm_inproj_fused_f16_noalloc": [P] + [P, sz] * 10 + [FusedInProjDims],
     "lssm_ssd_chunked_f16": [P] + [P, sz] * 9 + [SSDDims],
     "lssm_ssd_step_f16": [P] + [P, sz] * 9 + [SSDStepDims],
     "lssm_ssd_chunked_batched": [P] * 10 + [SSDBatchedDims],
