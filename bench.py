@@ -153,7 +153,29 @@ def allreduce_max(dist, vals, local):
     return t.tolist()
 
 
-def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=200):
+def graph_timed(ctx, stream, call, n, replays=4):
+    """Average device time of one `call` (a C-ABI op launch): the n calls are captured
+    once into a CUDA graph through the library's graph batching and the graph is
+    replayed, so the CUDA events measure kernels back to back, not host submission."""
+    import torch
+    ctx.set_graph_batching(True)
+    try:
+        ctx.begin_batch()
+        for i in range(n):
+            call(i)
+        ctx.commit_and_wait()          # instantiate + one warm run
+        ctx.replay_batch(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.replay_batch(replays)
+        e1.record(stream)
+        e1.synchronize()
+    finally:
+        ctx.set_graph_batching(False)
+    return e0.elapsed_time(e1) / (n * replays)
+
+
+def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=128):
     """Average device time of the dominant decode kernel (the in_proj INT4 GEMV,
     N = 10576, K = 2560) on layer 0's weights, CUDA events on the launching stream."""
     import ctypes as C
@@ -181,19 +203,7 @@ def time_kernel_int4_gemv(lssm, ctx, model, hp, reps=200):
         calls[0] += 1
         lssm.check(L.lssm_linear_int4_gemv(ctx.h, x.ptr, 0, base, off, base, off + N * dm // 2, y.ptr, 0, dims))
 
-    ctx.begin_batch()
-    for _ in range(10):
-        call()
-    ctx.commit_and_wait()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.begin_batch()
-    e0.record(stream)
-    for _ in range(reps):
-        call()
-    e1.record(stream)
-    ctx.commit_and_wait()
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+    ms = graph_timed(ctx, stream, lambda i: call(), reps)
     bytes_alg = nb + dm * 2 + N * 2
     _ = C
     return ms, bytes_alg
@@ -372,19 +382,7 @@ def run_kernel_bench(args):
     out = {"kernel": args.kernel}
 
     def timed(call, n):
-        ctx.begin_batch()
-        for i in range(min(n, 8)):
-            call(i)
-        ctx.commit_and_wait()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ctx.begin_batch()
-        e0.record(stream)
-        for i in range(n):
-            call(i)
-        e1.record(stream)
-        ctx.commit_and_wait()
-        e1.synchronize()
-        return e0.elapsed_time(e1) / n
+        return graph_timed(ctx, stream, call, n)
 
     if args.kernel in ("int4_gemv", "int4_gemv_out"):
         if args.kernel == "int4_gemv":

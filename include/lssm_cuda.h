@@ -88,6 +88,12 @@ const char* lssm_version(void);
 lssm_status lssm_begin_batch(lssm_ctx* ctx);
 lssm_status lssm_commit_and_wait(lssm_ctx* ctx);
 int lssm_batch_active(lssm_ctx* ctx);
+/* Graph batching (no reference counterpart; the Metal analogue is re-encoding a command
+ * buffer): when enabled, begin_batch captures the ops into a CUDA graph and commit_and_wait
+ * instantiates, runs and keeps it; lssm_replay_batch re-launches the kept graph `times` times
+ * on the context stream without waiting (same buffers and offsets as when captured). */
+lssm_status lssm_ctx_set_graph_batching(lssm_ctx* ctx, int enable);
+lssm_status lssm_replay_batch(lssm_ctx* ctx, uint32_t times);
 
 /* ---- device memory: replaces DeviceBuffer / UnifiedBuffer (include/lite_ssm/allocator.hpp:21-103)
  * There is no unified memory between an x86 host and a B200, so weights are copied

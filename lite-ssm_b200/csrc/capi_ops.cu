@@ -130,6 +130,9 @@ lssm_status lssm_ctx_create(int device, lssm_ctx** out) {
     if (e != cudaSuccess) { delete c; return cuda_fail(e, "lssm_ctx_create: stream"); }
     c->owns_stream = true;
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+    // The device error word of the bounded waits is allocated here, never lazily
+    // inside a later op (which might be running under stream capture).
+    if (!tc_error_word()) { lssm_ctx_destroy(c); return fail(LSSM_ERR_OUT_OF_MEMORY, "lssm_ctx_create: error word"); }
     *out = c;
     return LSSM_OK;
 }
@@ -138,6 +141,7 @@ lssm_status lssm_ctx_destroy(lssm_ctx* ctx) {
     if (!ctx) return LSSM_OK;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->last_graph) cudaGraphExecDestroy(ctx->last_graph);
     if (ctx->owns_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return LSSM_OK;
@@ -182,6 +186,11 @@ int lssm_has_kernel(const char* name) {
 lssm_status lssm_begin_batch(lssm_ctx* ctx) {
     CHECK_CTX(ctx);
     if (ctx->batch_active) return fail(LSSM_ERR_STATE, "MetalOps: begin_batch called while batch already active");
+    if (ctx->capture_batches) {
+        cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return cuda_fail(e, "begin_batch: stream capture");
+        ctx->capturing = true;
+    }
     ctx->batch_active = true;
     return LSSM_OK;
 }
@@ -190,7 +199,37 @@ lssm_status lssm_commit_and_wait(lssm_ctx* ctx) {
     CHECK_CTX(ctx);
     if (!ctx->batch_active) return fail(LSSM_ERR_STATE, "MetalOps: commit_and_wait without an active batch");
     ctx->batch_active = false;
+    if (ctx->capturing) {
+        ctx->capturing = false;
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+        if (e != cudaSuccess) return cuda_fail(e, "commit_and_wait: end capture");
+        if (ctx->last_graph) { cudaGraphExecDestroy(ctx->last_graph); ctx->last_graph = nullptr; }
+        e = cudaGraphInstantiate(&ctx->last_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { ctx->last_graph = nullptr; return cuda_fail(e, "commit_and_wait: instantiate"); }
+        e = cudaGraphLaunch(ctx->last_graph, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "commit_and_wait: graph launch");
+    }
     return finish_op(ctx, "forward batch");
+}
+
+lssm_status lssm_ctx_set_graph_batching(lssm_ctx* ctx, int enable) {
+    CHECK_CTX(ctx);
+    if (ctx->batch_active) return fail(LSSM_ERR_STATE, "set_graph_batching: a batch is active");
+    ctx->capture_batches = enable != 0;
+    return LSSM_OK;
+}
+
+lssm_status lssm_replay_batch(lssm_ctx* ctx, uint32_t times) {
+    CHECK_CTX(ctx);
+    if (!ctx->last_graph) return fail(LSSM_ERR_STATE, "replay_batch: no captured batch");
+    if (ctx->batch_active) return fail(LSSM_ERR_STATE, "replay_batch: a batch is active");
+    for (uint32_t i = 0; i < times; ++i) {
+        cudaError_t e = cudaGraphLaunch(ctx->last_graph, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "replay_batch");
+    }
+    return LSSM_OK;
 }
 
 int lssm_batch_active(lssm_ctx* ctx) { return ctx && ctx->batch_active ? 1 : 0; }

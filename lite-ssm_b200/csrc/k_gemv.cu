@@ -319,6 +319,126 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_int4_mma(const __half* __
     }
 }
 
+// ---------------------------------------------------------------------------
+//  INT4_B32 GEMV with TMA bulk staging (the decode hot kernel).
+//
+//  One CTA per 16-row tile. Before anything else one thread issues cp.async.bulk
+//  copies of the tile's 16 packed rows (K/2 bytes each, into rows padded by 16 B so
+//  the fragment reads below are bank-conflict free) and of the tile's contiguous
+//  scale block, all completing on one mbarrier. The whole tile (22.5 KB at K=2560)
+//  is in flight from a single instruction stream while the CTA stages (and
+//  optionally RMS-normalises) the activation vector; many resident CTAs per SM keep
+//  >100 KB per SM in flight, enough to cover HBM latency. The math is the same
+//  register-operand mma.sync dequant as k_gemv_int4_mma, reading words from shared
+//  memory instead of global.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool bar_wait_bounded(uint32_t bar, uint32_t parity) {
+    uint32_t ok = 0;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) return false;
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS) k_gemv_int4_tma(const __half* __restrict__ x,
+                                                              const uint8_t* __restrict__ packed,
+                                                              const __half* __restrict__ scales,
+                                                              __half* __restrict__ y, uint32_t M, uint32_t N,
+                                                              uint32_t K, const __half* __restrict__ norm_w,
+                                                              float eps, int* __restrict__ err) {
+    extern __shared__ __align__(128) uint8_t smem_gemv[];
+    __shared__ float red[32];
+    __shared__ float rr[GEMV_MMAX];
+    __shared__ float part[GEMV_WARPS][32][4];
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t nb = K / 32;
+    const uint32_t row_bytes = K / 2, row_stride = K / 2 + 16;
+    uint8_t* sW = smem_gemv;                                   // 16 rows, padded
+    __half* sS = reinterpret_cast<__half*>(sW + I4_ROWS * row_stride);   // 16 x nb scales
+    uint4* xs = reinterpret_cast<uint4*>(sS + I4_ROWS * nb);             // M x K/8 fragment quads
+    const uint32_t row0 = blockIdx.x * I4_ROWS;
+    const uint32_t nrows = min((uint32_t)I4_ROWS, N - row0);
+    const uint32_t bar_a = smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint32_t total = nrows * row_bytes + nrows * nb * 2;
+        asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(bar_a),
+                     "r"(total)
+                     : "memory");
+        for (uint32_t r = 0; r < nrows; ++r)
+            bulk_g2s(smem_u32(sW + r * row_stride), packed + (uint64_t)(row0 + r) * row_bytes, row_bytes, bar_a);
+        bulk_g2s(smem_u32(sS), scales + (uint64_t)row0 * nb, nrows * nb * 2, bar_a);
+    }
+    if (norm_w) prenorm_factors(x, M, K, eps, rr, red);
+    stage_x_frag(x, norm_w, rr, M, K, xs);
+    __syncthreads();
+    if (!bar_wait_bounded(bar_a, 0)) {
+        if (threadIdx.x == 0) atomicExch(err, 1);
+        return;
+    }
+
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, c = lane & 3;
+    const uint32_t ga = min(g, nrows - 1), gb = min(g + 8, nrows - 1);
+    const uint32_t* wa_row = reinterpret_cast<const uint32_t*>(sW + ga * row_stride) + c;
+    const uint32_t* wb_row = reinterpret_cast<const uint32_t*>(sW + gb * row_stride) + c;
+    const __half* sa = sS + ga * nb;
+    const __half* sb = sS + gb * nb;
+    const uint32_t b_begin = (nb * warp) / GEMV_WARPS, b_end = (nb * (warp + 1)) / GEMV_WARPS;
+    const bool has_x = g < M;
+    const uint4* xrow = xs + (uint64_t)(has_x ? g : 0) * (K / 8) + c;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+    for (uint32_t b = b_begin; b < b_end; ++b) {
+        const uint32_t wa = wa_row[b * 4], wb = wb_row[b * 4];
+        const uint4 xf = has_x ? xrow[b * 4] : make_uint4(0, 0, 0, 0);
+        uint32_t qa[4], qb[4];
+        dequant_word(wa, qa);
+        dequant_word(wb, qb);
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
+        const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
+        mma_16816(d, a1, xf.x, xf.y);
+        mma_16816(d, a2, xf.z, xf.w);
+        const float fa = __half2float(sa[b]), fb = __half2float(sb[b]);
+        acc[0] += d[0] * fa;
+        acc[1] += d[1] * fa;
+        acc[2] += d[2] * fb;
+        acc[3] += d[3] * fb;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) part[warp][lane][i] = acc[i];
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const uint32_t l = threadIdx.x >> 2, i = threadIdx.x & 3;
+        float t = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < GEMV_WARPS; ++w2) t += part[w2][l][i];
+        const uint32_t row = row0 + (l >> 2) + ((i & 2) ? 8 : 0);
+        const uint32_t m = (l & 3) * 2 + (i & 1);
+        if (row < N && m < M) gemv_store<EPI>(y, (uint64_t)m * N + row, t);
+    }
+}
+
+int* tc_error_word();
+
 // Fallback for layouts the vector kernel cannot address (unaligned packed rows):
 // one warp per row, lane = k within a block, like linear.metal:440-474.
 template <int EPI>
@@ -355,7 +475,12 @@ static cudaError_t gemv_int4_dispatch(const void* x, const void* packed, const v
     const __half* sp = static_cast<const __half*>(scales);
     const __half* np = static_cast<const __half*>(norm_w);
     __half* yp = static_cast<__half*>(y);
-    if (aligned(packed, 4) && aligned(scales, 2)) {
+    if (aligned(packed, 16) && aligned(scales, 16) && K % 256 == 0) {
+        const size_t smem = (size_t)I4_ROWS * (K / 2 + 16) + (size_t)I4_ROWS * (K / 32) * 2 + (size_t)M * K * 2;
+        auto k = k_gemv_int4_tma<EPI>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k<<<(N + I4_ROWS - 1) / I4_ROWS, GEMV_THREADS, smem, s>>>(xp, pp, sp, yp, M, N, K, np, eps, tc_error_word());
+    } else if (aligned(packed, 4) && aligned(scales, 2)) {
         const size_t smem = (size_t)M * K * 2;
         auto k = k_gemv_int4_mma<EPI>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

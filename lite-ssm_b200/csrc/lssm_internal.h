@@ -21,6 +21,11 @@ struct lssm_ctx {
     int sm_count = 148;
     // Device-side error word for bounded waits inside kernels (0 = ok).
     int* d_error = nullptr;
+    // Graph batching: when set, begin_batch starts a stream capture and
+    // commit_and_wait instantiates, launches and keeps the captured graph.
+    bool capture_batches = false;
+    bool capturing = false;
+    cudaGraphExec_t last_graph = nullptr;
 };
 
 namespace lssm {

@@ -77,6 +77,8 @@ _SIGS = {
     "lssm_ctx_set_stream": [P, P],
     "lssm_begin_batch": [P],
     "lssm_commit_and_wait": [P],
+    "lssm_ctx_set_graph_batching": [P, C.c_int],
+    "lssm_replay_batch": [P, u32],
     "lssm_alloc": [P, sz, C.POINTER(P)],
     "lssm_free": [P, P],
     "lssm_upload": [P, P, sz, P, sz],
@@ -203,6 +205,12 @@ class Ctx:
 
     def commit_and_wait(self):
         check(lib().lssm_commit_and_wait(self.h))
+
+    def set_graph_batching(self, enable: bool):
+        check(lib().lssm_ctx_set_graph_batching(self.h, 1 if enable else 0))
+
+    def replay_batch(self, times: int = 1):
+        check(lib().lssm_replay_batch(self.h, times))
 
     def batch_active(self) -> bool:
         return lib().lssm_batch_active(self.h) == 1

@@ -334,6 +334,30 @@ def test_ssd_chunked_batched_bf16_in_f32_out(ctx, ops, xdt):
     assert np.abs(s - se).max() <= 1e-4 * (1 + np.abs(se).max())
 
 
+def test_graph_batching_replay(ctx, ops):
+    """A captured batch replays the same ops on the same buffers (y += x, three times)."""
+    n = 3000
+    x = h(RNG.standard_normal(n))
+    bx, by = hb(ctx, x), hb(ctx, np.zeros(n, np.float16))
+    ctx.set_graph_batching(True)
+    ctx.begin_batch()
+    ops.add_inplace_f16((by, 0), (bx, 0), n)
+    ctx.commit_and_wait()            # runs once
+    ctx.replay_batch(2)              # twice more
+    ctx.set_graph_batching(False)
+    ctx.begin_batch()
+    ctx.commit_and_wait()            # plain batch: synchronises the stream
+    s = x.astype(np.float32)
+    ref = np.float16(np.float16(s + s) + s).astype(np.float32)
+    assert np.array_equal(get16(by, n), ref)
+    with pytest.raises(lssm.LssmError, match="a batch is active"):
+        ctx.begin_batch()
+        try:
+            ctx.set_graph_batching(True)
+        finally:
+            ctx.commit_and_wait()
+
+
 def test_batching_semantics(ctx, ops):
     n = 4096
     x = h(RNG.standard_normal(n))
