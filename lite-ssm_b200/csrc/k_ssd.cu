@@ -282,8 +282,14 @@ __global__ void __launch_bounds__(SSD_THREADS) k_ssd_chunked_simt(SsdArgs a) {
     for (uint32_t i = threadIdx.x; i < P * N; i += blockDim.x) Sg[i] = S[i];
 }
 
+cudaError_t launch_ssd_chunked_tc(const SsdArgs& s, cudaStream_t st);
+
 cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s) {
     if (!a.batch || !a.L || !a.H) return cudaSuccess;
+    // P = 64, N = 128 (every Mamba-2 checkpoint shape) with 16-byte aligned rows takes the
+    // tensor-core kernel; anything else uses the general-shape kernel below.
+    cudaError_t e = launch_ssd_chunked_tc(a, s);
+    if (e != cudaErrorNotSupported) return e;
     const size_t smem = sizeof(float) * ((size_t)a.P * a.N + 2ull * SSD_Q * a.N + (size_t)SSD_Q * a.P +
                                          (size_t)SSD_Q * SSD_Q + 3 * SSD_Q);
     if (smem > 220 * 1024) return cudaErrorInvalidValue;

@@ -297,12 +297,19 @@ def test_ssd_chunked_f16(ctx, ops, L, H, P, N, G, chunk):
     scale = np.abs(ye).max()
     assert np.abs(y - ye).max() <= 2e-3 * scale + 2e-3   # fp16 output rounding + fp32 accumulation
     s = bS.download(np.float32, H * P * N).reshape(1, H, P, N)
-    assert np.abs(s - se).max() <= 1e-4 * (1 + np.abs(se).max())
+    # P=64/N=128 shapes run on the tensor-core kernel, whose state update multiplies fp16
+    # operands (the decay-scaled B rows): a few fp16 ulps of max|S|.
+    assert np.abs(s - se).max() <= 3e-3 * (1 + np.abs(se).max())
 
 
-@pytest.mark.parametrize("xdt", [lssm.DT_BF16, lssm.DT_F16])
-def test_ssd_chunked_batched_bf16_in_f32_out(ctx, ops, xdt):
-    Bt, L, H, P, N, G = 2, 100, 4, 64, 128, 1
+@pytest.mark.parametrize("xdt,G,L", [(lssm.DT_BF16, 1, 100), (lssm.DT_F16, 1, 100), (lssm.DT_BF16, 2, 300),
+                                     (lssm.DT_F16, 2, 129)])
+def test_ssd_chunked_batched_bf16_in_f32_out(ctx, ops, xdt, G, L):
+    """P = 64, N = 128 runs on the tensor-core kernel: the intra-chunk weights M, the
+    scaled C / B rows and the state snapshot are MMA operands in the input dtype, so the
+    error vs the fp64 recurrence is a few input-dtype ulps of max|y| (bf16: 2^-8, fp16: 2^-11):
+    tolerance 1.5e-2 (bf16) / 3e-3 (fp16) of max|y|; the fp32 state carry is tighter."""
+    Bt, H, P, N = 2, 4, 64, 128
     r = np.random.default_rng(5)
     Xf = r.standard_normal((Bt, L, H, P)).astype(np.float32)
     Bf = r.standard_normal((Bt, L, G, N)).astype(np.float32)
@@ -329,9 +336,10 @@ def test_ssd_chunked_batched_bf16_in_f32_out(ctx, ops, xdt):
     ops.ssd_chunked_batched(*bufs, bY, bS, lssm.SSDBatchedDims(Bt, L, H, P, N, G, 256, 1e-6, 1e6, 1, xdt,
                                                                lssm.DT_F32, lssm.DT_F32, lssm.DT_F32))
     y = bY.download(np.float32, ye.size).reshape(ye.shape)
-    assert np.abs(y - ye).max() <= 1e-4 * (1 + np.abs(ye).max())
+    tol = 1.5e-2 if xdt == lssm.DT_BF16 else 3e-3
+    assert np.abs(y - ye).max() <= tol * np.abs(ye).max()
     s = bS.download(np.float32, se.size).reshape(se.shape)
-    assert np.abs(s - se).max() <= 1e-4 * (1 + np.abs(se).max())
+    assert np.abs(s - se).max() <= tol * np.abs(se).max()
 
 
 def test_graph_batching_replay(ctx, ops):
