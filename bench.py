@@ -324,7 +324,7 @@ def run_ours(args, world, rank, local, dist):
     prof = ROOT / "profiles" / "int4_gemv_inproj_traffic.json"
     traffic = json.loads(prof.read_text()).get("traffic_bytes_per_launch") if prof.exists() else None
     n_pre, n_dec = sess.launches()
-    launches = args.steps * (n_pre + (NEW - 1) * n_dec)
+    launches = args.steps * (n_pre + n_dec)   # n_dec: launches of the whole decode call
     prefill_flops = 2 * PROMPT * (HP27["n_layer"] * ((2 * 5120 + 256 + 80) * 2560 + 2560 * 5120))
 
     if rank == 0:

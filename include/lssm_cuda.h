@@ -248,10 +248,26 @@ lssm_status lssm_generate(lssm_session* s, const uint32_t* prompt, uint32_t L, u
 lssm_status lssm_session_logits(lssm_session* s, float* out);
 /* Device timing of the last prefill / decode call (CUDA events on the session stream), ms. */
 lssm_status lssm_session_timing(lssm_session* s, float* prefill_ms, float* decode_ms);
-/* Kernel launches issued by the last prefill and by one decode step. */
-lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* decode_step);
-/* Engine knobs: "cuda_graph" 1 = capture each decode step in a CUDA graph (default 1). */
+/* Kernel launches issued by the last prefill and by the last lssm_decode call (all its
+ * steps: 1 when the persistent decode kernel ran them). */
+lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* decode);
+/* Engine knobs (no reference counterpart; the reference has one decode path):
+ *   "persistent" 1 = run lssm_decode as one persistent cooperative kernel when the model
+ *                qualifies (batch <= 2, INT4_B32 in/out_proj, fp16 lm_head, d_state 128,
+ *                d_model and d_inner multiples of 256) (default 1);
+ *   "cuda_graph" 1 = otherwise capture each decode step in a CUDA graph (default 1);
+ *   "trace"      1 = record per-phase %globaltimer stamps of the persistent kernel's first
+ *                step (read with lssm_session_trace). */
 lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t value);
+/* Phase trace of the last persistent decode: sm_count x (n_layer * 10 + 6) u64 words.
+ * Per layer: [0] layer start, [1] in_proj RMSNorm staged, [2] in_proj + conv done,
+ * [3] after grid barrier, [4] ssd_step done, [5] after grid barrier, [6] out_proj RMSNorm
+ * staged, [7] out_proj done, [8] producer's first in_proj copy issued, [9] ns the CTA
+ * waited on its weight ring in this layer. Then lm_head: [0] norm staged, [1] logits +
+ * partial argmax done, [2] after grid barrier, [3] token chosen, [4] ns waited on the
+ * weight ring, [5] producer's first lm_head copy issued. With out = NULL only
+ * *n_out is set. */
+lssm_status lssm_session_trace(lssm_session* s, uint64_t* out, uint64_t cap, uint64_t* n_out);
 
 /* ---- host-only .ssm helpers (no device needed) ---------------------------
  * Plan the header + tensor index of a Mamba2ForCausalLM .ssm file exactly as

@@ -492,10 +492,21 @@ struct lssm_session {
     cudaEvent_t ev[4] = {};
     float prefill_ms = 0.0f, decode_ms = 0.0f;
     uint64_t nl = 0;                          // kernel launches issued (running count)
-    uint64_t prefill_launches = 0, decode_step_launches = 0;
+    uint64_t prefill_launches = 0, decode_step_launches = 0, decode_launches = 0;
     bool use_graph = true;
     cudaGraphExec_t graph = nullptr;
     bool logits_valid = false;
+    // persistent decode kernel (one launch for all decode steps) when the model allows it
+    bool persist_ok = false, use_persist = true;
+    PLayer* d_players = nullptr;
+    float* d_part_val = nullptr;
+    uint32_t* d_part_idx = nullptr;
+    uint32_t* d_bar = nullptr;
+    uint32_t seg_in = 0, seg_out = 0, seg_lm = 0;
+    void* d_maps = nullptr;        // CUtensorMap[4 * n_layer + 1]
+    const char* persist_why = "";  // why the persistent kernel is not used ("" = it is)
+    uint64_t* d_trace = nullptr;   // phase stamps of the persistent kernel's first step
+    bool trace_on = false;
 };
 
 static lssm_status s_alloc(void** p, size_t n, const char* what) {
@@ -510,13 +521,105 @@ extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
     cudaStreamSynchronize(s->ctx->stream);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
-                  s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err};
+                  s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
+                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps};
     for (void* p : ps)
         if (p) cudaFree(p);
     for (auto& e : s->ev)
         if (e) cudaEventDestroy(e);
     delete s;
     return LSSM_OK;
+}
+
+static size_t trace_words(const lssm_session* s) {
+    return (size_t)s->m->img.hdr.n_layer * TRACE_PER_LAYER + TRACE_LM;
+}
+
+// Decide whether the persistent decode kernel can run this model/batch (its shape plan,
+// INT4_B32 in/out_proj, fp16 lm_head, 16-byte aligned weights) and build its per-layer
+// pointer table and tensor maps. Anything else keeps the per-op graph path (the reason
+// is kept in persist_why).
+static lssm_status setup_persistent(lssm_session* s) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    s->persist_ok = false;
+    s->persist_why = "";
+    if (!tc_error_word()) { s->persist_why = "no device error word"; return LSSM_OK; }
+    PersistShape sh{h.n_layer, s->batch, h.d_model, m->d_inner, m->xbc, m->proj, h.n_heads, h.d_head,
+                    h.d_state, h.n_groups, h.d_conv, h.vocab_size, (uint32_t)s->ctx->sm_count};
+    const char* why = decode_persist_plan(sh, &s->seg_in, &s->seg_out, &s->seg_lm);
+    if (*why) { s->persist_why = why; return LSSM_OK; }
+    if (m->lm_head->dtype != DT_F16) { s->persist_why = "lm_head is not fp16"; return LSSM_OK; }
+    auto al = [&](const TensorRec* t) { return ((uintptr_t)(m->d_base + t->offset) % 16) == 0; };
+    if (!al(m->embed) || !al(m->norm_f) || !al(m->lm_head)) { s->persist_why = "unaligned tensor"; return LSSM_OK; }
+    for (auto& L : m->layers) {
+        if (L.in_proj->dtype != DT_INT4_B32 || L.out_proj->dtype != DT_INT4_B32) {
+            s->persist_why = "in_proj / out_proj not int4_b32";
+            return LSSM_OK;
+        }
+        if (!al(L.in_proj) || !al(L.out_proj) || !al(L.norm) || !al(L.mixer_norm)) {
+            s->persist_why = "unaligned tensor";
+            return LSSM_OK;
+        }
+    }
+    std::vector<PLayer> pl(h.n_layer);
+    for (uint32_t l = 0; l < h.n_layer; ++l) {
+        const LayerW& L = m->layers[l];
+        auto hp = [&](const TensorRec* t) { return reinterpret_cast<const __half*>(m->d_base + t->offset); };
+        pl[l].in_w = m->d_base + L.in_proj->offset;
+        pl[l].out_w = m->d_base + L.out_proj->offset;
+        pl[l].conv_w = hp(L.conv_w);
+        pl[l].conv_b = hp(L.conv_b);
+        pl[l].dt_bias = hp(L.dt_bias);
+        pl[l].A_log = hp(L.A_log);
+        pl[l].D = hp(L.D);
+        pl[l].norm_w = hp(L.norm);
+        pl[l].mixer_norm_w = hp(L.mixer_norm);
+        pl[l].conv_state = reinterpret_cast<__half*>(s->conv) + s->conv_layer * l;
+        pl[l].ssd_state = s->ssd + s->ssd_layer * l;
+    }
+    std::vector<uint8_t> maps(decode_persist_maps_bytes(h.n_layer));
+    if (!decode_persist_encode_maps(maps.data(), pl.data(), m->d_base + m->lm_head->offset, sh, s->seg_in, s->seg_out,
+                                    s->seg_lm)) {
+        s->persist_why = "tensor map encoding failed";
+        return LSSM_OK;
+    }
+    lssm_status st;
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_players), pl.size() * sizeof(PLayer), "session: layer table")))
+        return st;
+    if ((st = s_alloc(&s->d_maps, maps.size(), "session: tensor maps"))) return st;
+    const size_t parts = (size_t)s->ctx->sm_count * s->batch;
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_val), parts * 4, "session: argmax partials"))) return st;
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_idx), parts * 4, "session: argmax partials"))) return st;
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_bar), 16, "session: grid barrier"))) return st;
+    cudaError_t e = cudaMemcpy(s->d_players, pl.data(), pl.size() * sizeof(PLayer), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(s->d_maps, maps.data(), maps.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "session: persistent decode tables upload");
+    s->persist_ok = true;
+    return LSSM_OK;
+}
+
+static PParams persist_params(lssm_session* s, uint32_t n_steps) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    auto hp = [&](const TensorRec* t) { return reinterpret_cast<const __half*>(m->d_base + t->offset); };
+    PParams p{};
+    p.layers = s->d_players;
+    p.n_layer = h.n_layer;
+    p.embed = hp(m->embed);
+    p.norm_f = hp(m->norm_f);
+    p.lm_head = hp(m->lm_head);
+    p.hidden = s->hidden; p.projb = s->proj; p.xs = s->xs; p.Bs = s->Bs; p.Cs = s->Cs;
+    p.gated = s->gated; p.logits = s->logits;
+    p.part_val = s->d_part_val; p.part_idx = s->d_part_idx;
+    p.cur = s->d_cur; p.history = s->d_hist; p.hist_stride = s->hist_cap; p.n_steps = n_steps;
+    p.bar = s->d_bar; p.err = tc_error_word();
+    p.B = s->batch; p.dm = h.d_model; p.di = m->d_inner; p.xd = m->xbc; p.proj = m->proj;
+    p.H = h.n_heads; p.P = h.d_head; p.N = h.d_state; p.G = h.n_groups; p.dconv = h.d_conv; p.V = h.vocab_size;
+    p.maps = s->d_maps;
+    p.seg_in = s->seg_in; p.seg_out = s->seg_out; p.seg_lm = s->seg_lm;
+    p.trace = s->trace_on ? s->d_trace : nullptr;
+    return p;
 }
 
 extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_t batch, uint32_t max_L,
@@ -570,6 +673,7 @@ extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_
 #undef SA
     for (auto& e : s->ev) cudaEventCreate(&e);
     cudaMemsetAsync(s->d_err, 0, 16, ctx->stream);
+    if ((st = setup_persistent(s.get()))) return st;
     if ((st = lssm_session_reset(s.get()))) return st;
     *out = s.release();
     return LSSM_OK;
@@ -589,6 +693,19 @@ extern "C" lssm_status lssm_session_reset(lssm_session* s) {
 
 extern "C" lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t value) {
     if (!s || !key) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_set_option: null argument");
+    if (std::strcmp(key, "persistent") == 0) {
+        s->use_persist = value != 0;
+        return LSSM_OK;
+    }
+    if (std::strcmp(key, "trace") == 0) {
+        s->trace_on = value != 0;
+        if (s->trace_on && !s->d_trace && s->persist_ok) {
+            const size_t n = (size_t)s->ctx->sm_count * trace_words(s);
+            if (lssm_status st = s_alloc(reinterpret_cast<void**>(&s->d_trace), n * 8, "session: trace")) return st;
+            cudaMemset(s->d_trace, 0, n * 8);
+        }
+        return LSSM_OK;
+    }
     if (std::strcmp(key, "cuda_graph") == 0) {
         s->use_graph = value != 0;
         if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
@@ -792,6 +909,26 @@ extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint3
     }
     CU(cudaMemcpyAsync(s->d_cur, first, (size_t)s->batch * 4, cudaMemcpyHostToDevice, st));
     CU(cudaMemsetAsync(s->d_step, 0, 4, st));
+    if (s->persist_ok && s->use_persist) {
+        // one cooperative launch runs all n_steps tokens (embedding gather included);
+        // the kernel reads embedding rows directly, so the ids are range-checked here
+        for (uint32_t b = 0; b < s->batch; ++b)
+            if (first[b] >= h.vocab_size)
+                return fail(LSSM_ERR_INVALID_ARGUMENT, "Mamba2Model::embed: token_id out of range (decode)");
+        CU(cudaMemsetAsync(s->d_bar, 0, 4, st));
+        PParams pp = persist_params(s, n_steps);
+        CU(cudaEventRecord(s->ev[2], st));
+        CU(launch_decode_persist(pp, s->ctx->sm_count, st));
+        CU(cudaEventRecord(s->ev[3], st));
+        s->decode_launches = 1;
+        if (out_tokens)
+            CU(cudaMemcpy2DAsync(out_tokens, (size_t)n_steps * 4, s->d_hist, (size_t)s->hist_cap * 4, (size_t)n_steps * 4,
+                                 s->batch, cudaMemcpyDeviceToHost, st));
+        CU(cudaStreamSynchronize(st));
+        cudaEventElapsedTime(&s->decode_ms, s->ev[2], s->ev[3]);
+        s->logits_valid = true;
+        return check_err(s, "decode");
+    }
     CU(launch_embed_gather(s->d_cur, W(m, m->embed), s->hidden, s->batch, h.d_model, h.vocab_size, s->d_err, st));
     if (s->use_graph && !s->graph) {
         cudaGraph_t g;
@@ -816,6 +953,7 @@ extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint3
         }
     }
     CU(cudaEventRecord(s->ev[3], st));
+    s->decode_launches = 1 + (uint64_t)n_steps * s->decode_step_launches;
     if (out_tokens) {
         // history is (batch, hist_cap); copy the first n_steps of each row
         CU(cudaMemcpy2DAsync(out_tokens, (size_t)n_steps * 4, s->d_hist, (size_t)s->hist_cap * 4, (size_t)n_steps * 4,
@@ -864,10 +1002,26 @@ extern "C" lssm_status lssm_session_logits(lssm_session* s, float* out) {
     return LSSM_OK;
 }
 
+extern "C" lssm_status lssm_session_trace(lssm_session* s, uint64_t* out, uint64_t cap, uint64_t* n_out) {
+    if (!s || !n_out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_trace: null argument");
+    *n_out = 0;
+    if (!s->persist_ok)
+        return fail(LSSM_ERR_STATE, "lssm_session_trace: the persistent decode kernel does not run this session (%s)",
+                    s->persist_why);
+    if (!s->d_trace) return fail(LSSM_ERR_STATE, "lssm_session_trace: tracing is off");
+    const size_t n = (size_t)s->ctx->sm_count * trace_words(s);
+    *n_out = n;
+    if (!out) return LSSM_OK;
+    if (cap < n) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_trace: buffer holds %llu words, %zu needed",
+                             (unsigned long long)cap, n);
+    CU(cudaMemcpy(out, s->d_trace, n * 8, cudaMemcpyDeviceToHost));
+    return LSSM_OK;
+}
+
 extern "C" lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* decode_step) {
     if (!s) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_launches: null session");
     if (prefill) *prefill = s->prefill_launches;
-    if (decode_step) *decode_step = s->decode_step_launches;
+    if (decode_step) *decode_step = s->decode_launches;
     return LSSM_OK;
 }
 

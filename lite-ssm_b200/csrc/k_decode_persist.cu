@@ -1,0 +1,866 @@
+// k_decode_persist.cu — the whole greedy decode loop (all layers, lm_head, argmax,
+// next-token embedding) as ONE persistent cooperative kernel: one CTA per SM,
+// `n_steps` tokens per launch. Restates the decode half of the reference's
+// generate() loop (src/runtime/inference.cpp:55-67: embed -> forward_step ->
+// compute_logits -> sample_greedy) for batch <= 2 with INT4_B32 in/out_proj and an
+// fp16 lm_head, the 2.7B-shaped headline workload.
+//
+// Why one kernel: a batch-1 decode token streams 2.05 GB of weights and state in
+// ~0.32 ms at HBM speed, while a kernel-per-op step has ~260 launches whose ramp-up,
+// tail and launch gaps cost several times that. Here:
+//   * warp 7 is the TMA producer: it walks this CTA's weight chunks for every layer
+//     and token in order and streams each chunk (16 rows x seg * 128 bytes, plus the
+//     INT4 scales) with ONE tensor-map copy (128-byte swizzle, L2 evict-first) into
+//     an 11-stage shared-memory ring, and bulk-copies this CTA's rows of the layer's
+//     ssd state into a separate buffer. Weights do not depend on activations, so it
+//     runs ahead across phase boundaries and grid barriers: HBM stays busy while the
+//     consumers synchronise.
+//   * warps 0..6 consume. Each warp releases a ring slot as soon as it has read it;
+//     a CTA's tiles of a phase are accumulated in registers in groups of up to 5 and
+//     reduced across warps once per group. Per layer:
+//       A  RMSNorm(hidden) staged in MMA-fragment order, in_proj INT4 GEMV on
+//          register-operand mma.sync (the dequantisation of k_gemv.cu), epilogue:
+//          z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
+//          (each epilogue thread loaded its conv weights / state at layer start)
+//       -- grid barrier --
+//       B  ssd_step + gate on the CTA's state rows (already in shared memory), with
+//          B / C vectors and per-row scalars staged in one parallel round of loads:
+//          S = e^{A dt} S + dt B x, y = C.S + D x, gated = half(silu(z) * half(y))
+//       -- grid barrier --
+//       C  RMSNorm(gated) staged, out_proj INT4 GEMV, residual add into hidden (each
+//          epilogue thread keeps its hidden element in a register across layers)
+//       -- grid barrier --
+//     then norm_f + lm_head (fp16 weights, mma.sync), per-CTA first-max argmax
+//     partials, a grid barrier, and every CTA reduces the partials to the same next
+//     token (no host round-trip; the next token's embedding row is read directly).
+// The tile -> CTA assignment (tile t to CTA t mod grid) is the same in every layer
+// and step, so the rows a CTA owns (conv state, ssd state, hidden) are only ever
+// written by that CTA.
+// Grid barriers are a monotonically increasing global counter (release add, acquire
+// spin) with a 2 s %globaltimer bound; every mbarrier wait is bounded too. A timeout
+// sets the error word and all CTAs leave after draining their in-flight copies.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <vector>
+
+#include "device_util.cuh"
+#include "lssm_internal.h"
+#include "mma_int4.cuh"
+
+namespace lssm {
+
+namespace {
+
+// 7 consumer warps + 1 producer warp: with 8 warps each SM sub-partition holds two,
+// so the kernel may use up to 255 registers per thread (a 9th warp caps it at 168).
+constexpr int CONS_WARPS = 7, CONS = CONS_WARPS * 32, THREADS = CONS + 32;
+constexpr int RING = 11;
+constexpr uint32_t STAGE = 12288;                         // 1024-aligned (128-byte swizzle atoms)
+constexpr uint32_t SEG_MAX = 5;                           // 16 x 5 x 128 B + INT4 scales <= STAGE
+constexpr uint32_t TG = 5;                                // tiles per register-accumulated group
+constexpr uint32_t XBUF = 20480;                          // staged activation (<= 2 x 5120 halves)
+constexpr uint32_t PART = TG * CONS_WARPS * 32 * 4 * 4;   // per-warp partial sums of one group
+constexpr uint32_t SBUF = 36864;                          // this CTA's ssd state rows (<= 72 x 128 fp32)
+constexpr uint32_t SROWS = SBUF / 512;
+constexpr uint32_t BSLOTS = 4;                            // (seq, head) B / C vector slots in phase B
+constexpr uint32_t LT_MAX = 64;                           // layers whose table entries fit in smem
+constexpr uint32_t OFF_RING = 0;
+constexpr uint32_t OFF_X = OFF_RING + RING * STAGE;
+constexpr uint32_t OFF_PART = OFF_X + XBUF;
+constexpr uint32_t OFF_S = OFF_PART + PART;
+constexpr uint32_t OFF_BC = OFF_S + SBUF;                 // BSLOTS x {B, C} x 128 halves
+constexpr uint32_t OFF_ROWV = OFF_BC + BSLOTS * 512;      // SROWS x 5 floats
+constexpr uint32_t OFF_LT = OFF_ROWV + SROWS * 5 * 4;     // layer table
+constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
+constexpr uint32_t N_BARS = 2 * RING + 2;
+constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[16], tok[2], abort, arg v[16] / i[16]
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 256;
+constexpr uint64_t SPIN_NS = 2000000000ull;
+static_assert(SMEM_BYTES <= 232448, "persistent decode kernel exceeds 227 KB of shared memory");
+static_assert(sizeof(PLayer) % 8 == 0 && OFF_BAR % 8 == 0, "layer table / barriers misaligned");
+static_assert(SEG_MAX * 16 * (128 + 16) <= STAGE, "INT4 chunk does not fit a stage");
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONS) : "memory"); }
+__device__ __forceinline__ void mbar_init1(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(bar),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Phase wait: the common case (already complete) costs one try_wait; the clock is
+// read only once the wait actually blocks. Gives up on the CTA abort flag or after 2 s.
+__device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (true) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort) return false;
+        if (gtimer() - t0 > SPIN_NS) { *abort = 1; return false; }
+    }
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                                     uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma2(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint32_t bar,
+                                     uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
+        : "memory");
+}
+
+// Grid barrier over the consumer threads of every CTA (the producer warp never joins).
+__device__ __forceinline__ bool grid_sync(const PParams& p, uint32_t& gen, volatile int* abort) {
+    cons_sync();
+    if (threadIdx.x == 0) {
+        gen += 1;
+        asm volatile("fence.acq_rel.gpu;\n red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+        const uint32_t target = gen * gridDim.x;
+        uint64_t t0 = 0;
+        for (uint32_t it = 1;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
+            if ((int32_t)(v - target) >= 0) break;
+            if ((it & 31) == 0) {
+                if (*abort) break;
+                if (*reinterpret_cast<volatile int*>(p.err)) { *abort = 1; break; }   // another CTA gave up
+                const uint64_t t = gtimer();
+                if (!t0) t0 = t;
+                else if (t - t0 > SPIN_NS) { *abort = 1; atomicExch(p.err, 1); break; }
+            }
+        }
+    }
+    cons_sync();
+    return !*abort;
+}
+
+// Swizzled shared-memory offset of 16-byte chunk `j` (0..7) of 128-byte segment `s` of
+// tile row `r` (rows of seg segments): the tensor map's 128-byte swizzle XORs the chunk
+// index with the row's 128-byte line index mod 8. With an odd seg the 8 rows an MMA
+// fragment reads land on 8 different chunk positions (no bank conflicts).
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, uint32_t j) {
+    const uint32_t line = r * seg + s;
+    return line * 128 + ((j ^ (line & 7)) << 4);
+}
+
+// INT4 chunk (16 rows x seg*256 k): this warp's share of the chunk's 32-wide blocks.
+// x is staged over the whole K in fragment order (4 uint4 per 32-k block).
+__device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
+                                             uint32_t K8, uint32_t M, float acc[4]) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, c = lane & 3;
+    const uint32_t nb = seg * 8;
+    const __half* sc = reinterpret_cast<const __half*>(stage + 16 * seg * 128);
+    const __half* sa = sc + g * nb;
+    const __half* sbp = sc + (g + 8) * nb;
+    const bool has_x = g < M;
+    const uint4* xrow = xs + (uint64_t)(has_x ? g : 0) * K8 + (uint64_t)chunk * nb * 4 + c;
+    const uint32_t b0 = (nb * warp) / CONS_WARPS, b1 = (nb * (warp + 1)) / CONS_WARPS;
+    // Fully unrolled over the warp's (at most MAXB) blocks so their load -> dequant ->
+    // mma chains overlap: at one CTA per SM the GEMV is latency-bound otherwise.
+    constexpr uint32_t MAXB = (SEG_MAX * 8 + CONS_WARPS - 1) / CONS_WARPS;
+#pragma unroll
+    for (uint32_t i = 0; i < MAXB; ++i) {
+        const uint32_t b = b0 + i;
+        if (b >= b1) break;
+        const uint32_t s = b >> 3, j = b & 7;
+        const uint4 xf = has_x ? xrow[b * 4] : make_uint4(0, 0, 0, 0);
+        const uint32_t wa = *reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j) + 4 * c);
+        const uint32_t wb = *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j) + 4 * c);
+        uint32_t qa[4], qb[4];
+        dequant_word(wa, qa);
+        dequant_word(wb, qb);
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
+        const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
+        mma_16816(d, a1, xf.x, xf.y);
+        mma_16816(d, a2, xf.z, xf.w);
+        const float fa = __half2float(sa[b]), fb = __half2float(sbp[b]);
+        acc[0] += d[0] * fa;
+        acc[1] += d[1] * fa;
+        acc[2] += d[2] * fb;
+        acc[3] += d[3] * fb;
+    }
+}
+
+// fp16 chunk (lm_head, 16 rows x seg*64 k): this warp's share of the 16-wide k steps.
+__device__ __forceinline__ void consume_f16(const uint8_t* stage, uint32_t seg, uint32_t chunk, const __half* xh,
+                                            uint32_t K, uint32_t M, float acc[4]) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, c = lane & 3;
+    const uint32_t nks = seg * 4;
+    const bool has_x = g < M;
+    const __half* xr = xh + (uint64_t)(has_x ? g : 0) * K + (uint64_t)chunk * seg * 64;
+    const uint32_t k0 = (nks * warp) / CONS_WARPS, k1 = (nks * (warp + 1)) / CONS_WARPS;
+    constexpr uint32_t MAXK = (SEG_MAX * 4 + CONS_WARPS - 1) / CONS_WARPS;
+#pragma unroll
+    for (uint32_t i = 0; i < MAXK; ++i) {
+        const uint32_t ks = k0 + i;
+        if (ks >= k1) break;
+        const uint32_t s = ks >> 2, j = (ks & 3) * 2;
+        const uint32_t a[4] = {*reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j) + 4 * c),
+                               *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j) + 4 * c),
+                               *reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j + 1) + 4 * c),
+                               *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j + 1) + 4 * c)};
+        const uint32_t xb0 = has_x ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c) : 0u;
+        const uint32_t xb1 = has_x ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c + 8) : 0u;
+        mma_16816(acc, a, xb0, xb1);
+    }
+}
+
+// RMSNorm of M <= 2 rows of `src` (length K, K % 8 == 0, K / 8 <= 3 * CONS) with weight
+// w -> staged fp16 values (rmsnorm_f16 arithmetic, shaders/norm.metal:51-79); `frag`
+// selects the INT4 MMA fragment permutation (quads x[8q + {0,4,1,5,2,6,3,7}]). Each
+// thread owns up to 3 octets of each row, loaded once (with the weights) as 16-byte
+// vectors through L2 (other CTAs wrote the rows); both rows' loads are issued before
+// either reduction.
+__device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_t* tok, const __half* embed,
+                           const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* red) {
+    const uint32_t tid = threadIdx.x, nq = K / 8;
+    uint4 xv[2][3], wv[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const uint32_t q = tid + i * CONS;
+        if (q < nq) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + q);
+    }
+#pragma unroll
+    for (uint32_t m = 0; m < 2; ++m) {
+        if (m >= M) break;
+        const __half* xr = tok ? embed + (uint64_t)tok[m] * K : src + (uint64_t)m * src_stride;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint32_t q = tid + i * CONS;
+            if (q < nq) xv[m][i] = __ldcg(reinterpret_cast<const uint4*>(xr) + q);
+        }
+    }
+#pragma unroll
+    for (uint32_t m = 0; m < 2; ++m) {
+        if (m >= M) break;
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            if (tid + i * CONS < nq) {
+                const __half2* h2 = reinterpret_cast<const __half2*>(&xv[m][i]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __half22float2(h2[j]);
+                    ss += f.x * f.x + f.y * f.y;
+                }
+            }
+        }
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[m * 8 + (tid >> 5)] = ss;
+    }
+    cons_sync();
+#pragma unroll
+    for (uint32_t m = 0; m < 2; ++m) {
+        if (m >= M) break;
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CONS_WARPS; ++i) tot += red[m * 8 + i];
+        const float rr = rsqrtf(tot / (float)K + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint32_t q = tid + i * CONS;
+            if (q >= nq) continue;
+            const __half* xh8 = reinterpret_cast<const __half*>(&xv[m][i]);
+            const __half* wh8 = reinterpret_cast<const __half*>(&wv[i]);
+            __half v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(xh8[j]) * __half2float(wh8[j]) * rr);
+            uint4 u;
+            if (frag) {
+                __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
+                __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
+                u.x = *reinterpret_cast<uint32_t*>(&o0);
+                u.y = *reinterpret_cast<uint32_t*>(&o1);
+                u.z = *reinterpret_cast<uint32_t*>(&o2);
+                u.w = *reinterpret_cast<uint32_t*>(&o3);
+            } else {
+                u = *reinterpret_cast<uint4*>(v);
+            }
+            reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
+        }
+    }
+    cons_sync();
+}
+
+// First-max argmax step: (v, i) replaces (bv, bi) when larger, or equal with a lower index.
+__device__ __forceinline__ void argmax_take(float& bv, uint32_t& bi, float v, uint32_t i) {
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+// Warp-wide first-max over lanes of the same sequence (lane % B), B in {1, 2}.
+__device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
+    for (uint32_t off = 16; off >= B; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, i, off);
+        argmax_take(v, i, ov, oi);
+    }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* empty = full + RING;
+    uint64_t* sfull = empty + RING;       // ssd state rows landed
+    uint64_t* sempty = sfull + 1;         // ssd state buffer released by the consumers
+    float* red = reinterpret_cast<float*>(smem + OFF_MISC);              // 2 x 8 floats
+    uint32_t* tok = reinterpret_cast<uint32_t*>(red + 16);                 // 2 tokens
+    volatile int* abort = reinterpret_cast<volatile int*>(tok + 2);
+    float* argv = reinterpret_cast<float*>(smem + OFF_MISC + 128);         // 16 floats
+    uint32_t* argi = reinterpret_cast<uint32_t*>(argv + 16);              // 16 ids
+    PLayer* LT = reinterpret_cast<PLayer*>(smem + OFF_LT);
+    float* part = reinterpret_cast<float*>(smem + OFF_PART);
+    uint8_t* xbuf = smem + OFF_X;
+    const float* sstate = reinterpret_cast<const float*>(smem + OFF_S);
+    __half* bcs = reinterpret_cast<__half*>(smem + OFF_BC);
+    float* rowv = reinterpret_cast<float*>(smem + OFF_ROWV);
+    const CUtensorMap* maps = static_cast<const CUtensorMap*>(p.maps);
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint32_t nA = (p.proj + 15) / 16, nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
+    const uint32_t ntA = cta < nA ? (nA - 1 - cta) / G + 1 : 0;   // this CTA's tiles per phase
+    const uint32_t ntC = cta < nC ? (nC - 1 - cta) / G + 1 : 0;
+    const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;
+    const uint32_t srows = p.B * p.H * p.P;
+    const uint32_t r0 = (uint32_t)(((uint64_t)srows * cta) / G), r1 = (uint32_t)(((uint64_t)srows * (cta + 1)) / G);
+    const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
+
+    // Shapes the host checks before choosing this kernel, re-checked (identically in
+    // every CTA) so a bad launch reports an error instead of overrunning shared memory.
+    if (((nA + G - 1) / G) * 16 * p.B > CONS || ((nC + G - 1) / G) * 16 * p.B > CONS || p.dconv > 4 || p.dconv < 1 ||
+        p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || (srows + G - 1) / G > SROWS || p.n_layer > LT_MAX ||
+        (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || p.dm / 8 > 3 * CONS || p.di / 8 > 3 * CONS ||
+        p.seg_in > SEG_MAX || p.seg_out > SEG_MAX || p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) ||
+        !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm || nchC * p.seg_out * 256 != p.di ||
+        nchL * p.seg_lm * 64 != p.dm) {
+        if (tid == 0) atomicExch(p.err, 1);
+        return;
+    }
+
+    if (tid == 0) {
+        for (int s = 0; s < RING; ++s) {
+            mbar_init1(smem_u32(&full[s]), 1);
+            mbar_init1(smem_u32(&empty[s]), CONS_WARPS);
+        }
+        mbar_init1(smem_u32(sfull), 1);
+        mbar_init1(smem_u32(sempty), 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (tid < p.B) tok[tid] = p.cur[tid];
+    for (uint32_t i = tid; i < p.n_layer * (uint32_t)(sizeof(PLayer) / 8); i += THREADS)
+        reinterpret_cast<uint64_t*>(LT)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
+    __syncthreads();
+
+    const uint64_t tbase = (uint64_t)cta * (p.n_layer * TRACE_PER_LAYER + TRACE_LM);
+    const uint32_t lmb = p.n_layer * TRACE_PER_LAYER;
+
+    if (tid >= CONS) {
+        // ------------------------------------------------------------ producer
+        if (tid == CONS) {
+            const uint64_t pol = evict_first_policy();
+            uint32_t slot = 0, phase = 0, sphase = 0;
+            int last_phase[RING];
+            for (int s = 0; s < RING; ++s) last_phase[s] = -1;
+            bool state_issued = false;
+            auto take = [&]() -> uint32_t {   // next free stage (bounded wait); ~0u on abort
+                if (!mbar_wait_ab(smem_u32(&empty[slot]), phase ^ 1, abort)) return ~0u;
+                return slot;
+            };
+            auto advance = [&]() {
+                last_phase[slot] = (int)phase;
+                if (++slot == RING) { slot = 0; phase ^= 1; }
+            };
+            const uint32_t sbytes = (r1 - r0) * p.N * 4;
+            bool ok = true;
+            for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
+                for (uint32_t l = 0; l < p.n_layer && ok; ++l) {
+                    const CUtensorMap* mp = maps + 4 * l;
+                    for (uint32_t ti = 0; ti < ntA && ok; ++ti)
+                        for (uint32_t c = 0; c < nchA && ok; ++c) {
+                            const uint32_t s = take();
+                            if (s == ~0u) { ok = false; break; }
+                            const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
+                            const int32_t row0 = (int32_t)((cta + ti * G) * 16);
+                            mbar_expect(bar, 16 * p.seg_in * (128 + 16));
+                            tma3(dst, mp + 0, 0, (int32_t)(c * p.seg_in), row0, bar, pol);
+                            tma2(dst + 16 * p.seg_in * 128, mp + 1, (int32_t)(c * p.seg_in * 8), row0, bar, pol);
+                            advance();
+                            if (p.trace && step == 0 && ti == 0 && c == 0)
+                                p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
+                        }
+                    if (!ok) break;
+                    // this layer's ssd state rows, once the previous layer's are released
+                    if (!mbar_wait_ab(smem_u32(sempty), sphase ^ 1, abort)) { ok = false; break; }
+                    if (sbytes) {
+                        mbar_expect(smem_u32(sfull), sbytes);
+                        bulk_g2s(smem_u32(smem + OFF_S), LT[l].ssd_state + (uint64_t)r0 * p.N, sbytes, smem_u32(sfull));
+                    } else {
+                        mbar_arrive1(smem_u32(sfull));
+                    }
+                    state_issued = true;
+                    sphase ^= 1;
+                    for (uint32_t ti = 0; ti < ntC && ok; ++ti)
+                        for (uint32_t c = 0; c < nchC && ok; ++c) {
+                            const uint32_t s = take();
+                            if (s == ~0u) { ok = false; break; }
+                            const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
+                            const int32_t row0 = (int32_t)((cta + ti * G) * 16);
+                            mbar_expect(bar, 16 * p.seg_out * (128 + 16));
+                            tma3(dst, mp + 2, 0, (int32_t)(c * p.seg_out), row0, bar, pol);
+                            tma2(dst + 16 * p.seg_out * 128, mp + 3, (int32_t)(c * p.seg_out * 8), row0, bar, pol);
+                            advance();
+                        }
+                }
+                const CUtensorMap* ml = maps + 4 * p.n_layer;
+                for (uint32_t ti = 0; ti < ntL && ok; ++ti)
+                    for (uint32_t c = 0; c < nchL && ok; ++c) {
+                        const uint32_t s = take();
+                        if (s == ~0u) { ok = false; break; }
+                        const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
+                        mbar_expect(bar, 16 * p.seg_lm * 128);
+                        tma3(dst, ml, 0, (int32_t)(c * p.seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
+                        advance();
+                        if (p.trace && step == 0 && ti == 0 && c == 0) p.trace[tbase + lmb + 5] = gtimer();
+                    }
+            }
+            // every issued copy must land before the CTA exits (bounded)
+            for (int s = 0; s < RING; ++s)
+                if (last_phase[s] >= 0) bar_wait_bounded(smem_u32(&full[s]), (uint32_t)last_phase[s]);
+            if (state_issued) bar_wait_bounded(smem_u32(sfull), sphase ^ 1);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    uint32_t slot = 0, phase = 0, gen = 0, sphase = 0;
+    uint64_t wait_ns = 0;   // trace: warp 0's time blocked on the ring in this layer
+
+    // Consume `nt` (<= TG) consecutive tiles of this CTA: all their chunks, accumulated
+    // per tile in registers; then every warp's partial sums go to shared memory
+    // (readable after the closing barrier).
+    auto consume_group = [&](bool int4, uint32_t seg, uint32_t nch, uint32_t K, uint32_t nt) -> bool {
+        float acc[TG][4];
+#pragma unroll
+        for (uint32_t ti = 0; ti < TG; ++ti) {
+            acc[ti][0] = acc[ti][1] = acc[ti][2] = acc[ti][3] = 0.0f;
+            if (ti < nt) {
+                for (uint32_t c = 0; c < nch; ++c) {
+                    const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
+                    if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) return false;
+                    if (p.trace && tid == 0) wait_ns += gtimer() - w0;
+                    const uint8_t* stage = smem + OFF_RING + slot * STAGE;
+                    if (int4) consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), K / 8, p.B, acc[ti]);
+                    else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, p.B, acc[ti]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
+                    if (++slot == RING) { slot = 0; phase ^= 1; }
+                }
+            }
+        }
+#pragma unroll
+        for (uint32_t ti = 0; ti < TG; ++ti)
+            if (ti < nt)
+                *reinterpret_cast<float4*>(part + ((ti * CONS_WARPS + warp) * 32 + lane) * 4) =
+                    make_float4(acc[ti][0], acc[ti][1], acc[ti][2], acc[ti][3]);
+        cons_sync();
+        return true;
+    };
+    // Cross-warp sum of output (tile ordinal ti within the group, row, m): the m16n8
+    // accumulator of lane (g, c) holds rows g / g + 8 and columns (sequences) 2c, 2c + 1.
+    auto reduce_item = [&](uint32_t ti, uint32_t row, uint32_t m) -> float {
+        const uint32_t src = (row & 7) * 4 + (m >> 1), idx = (m & 1) + ((row >> 3) << 1);
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < CONS_WARPS; ++w) s += part[((ti * CONS_WARPS + w) * 32 + src) * 4 + idx];
+        return s;
+    };
+
+    // Each thread owns one (tile ordinal, row, seq) output of in_proj and of out_proj.
+    const uint32_t tiA = tid / (16 * p.B), rowA = (tid / p.B) % 16, mA = tid % p.B;
+    const bool ownA = tiA < ntA;
+    const uint32_t rA = (cta + tiA * G) * 16 + rowA;           // in_proj output row
+    const bool convA = ownA && rA >= p.di && rA < p.di + p.xd;
+    const uint32_t dA = rA - p.di;
+    const uint32_t tiC = tid / (16 * p.B), rowC = (tid / p.B) % 16, mC = tid % p.B;
+    const bool ownC = tiC < ntC;
+    const uint32_t rC = (cta + tiC * G) * 16 + rowC;           // out_proj output row (hidden index)
+    float hreg = 0.0f;                                         // hidden[mC][rC], carried across layers
+
+    const uint32_t GN = p.G * p.N, hpg = p.H / p.G;
+    bool ok = true;
+    for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
+        const bool tr = p.trace && step == 0 && tid == 0;
+        auto stamp = [&](uint32_t idx) {
+            if (tr) p.trace[tbase + idx] = gtimer();
+        };
+        for (uint32_t l = 0; l < p.n_layer && ok; ++l) {
+            const PLayer& L = LT[l];
+            const uint32_t lb = l * TRACE_PER_LAYER;
+            stamp(lb + 0);
+            wait_ns = 0;
+            // ---- loads consumed only in this layer's epilogues (issued first, waited late)
+            // (kept as raw fp16 bits until the epilogue so no conversion waits on them)
+            __half cwh[4], csh[4], cbh = __ushort_as_half(0);
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) cwh[k] = csh[k] = __ushort_as_half(0);
+            if (convA) {
+                const __half* wrow = L.conv_w + (uint64_t)dA * p.dconv;
+                const __half* srow = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
+#pragma unroll
+                for (uint32_t k = 0; k < 4; ++k)
+                    if (k < p.dconv) { cwh[k] = wrow[k]; csh[k] = srow[k]; }
+                cbh = L.conv_b[dA];
+            }
+            __half h0 = __ushort_as_half(0);
+            if (l == 0 && ownC && rC < p.dm) h0 = p.embed[(uint64_t)tok[mC] * p.dm + rC];
+            if (l == 0) hreg = __half2float(h0);
+            // ---- A: RMSNorm + in_proj + conv/SiLU/split
+            stage_norm(p.hidden, p.dm, l == 0 ? tok : nullptr, p.embed, L.norm_w, p.B, p.dm, true, xbuf, red);
+            stamp(lb + 1);
+            for (uint32_t g0 = 0; g0 < ntA && ok; g0 += TG) {
+                const uint32_t nt = min(TG, ntA - g0);
+                if (!consume_group(true, p.seg_in, nchA, p.dm, nt)) { ok = false; break; }
+                if (ownA && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
+                    const __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
+                    if (!convA) {
+                        p.projb[(uint64_t)mA * p.proj + rA] = vh;          // z or dt
+                    } else {
+                        // conv-state roll + depthwise conv + SiLU (k_conv_update_silu_split arithmetic)
+                        __half* st = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
+                        float acc = __half2float(cbh);
+#pragma unroll
+                        for (uint32_t k = 0; k < 3; ++k)
+                            if (k + 1 < p.dconv) {
+                                st[k] = csh[k + 1];
+                                acc += __half2float(csh[k + 1]) * __half2float(cwh[k]);
+                            }
+                        st[p.dconv - 1] = vh;
+                        __half wl = cwh[0];
+#pragma unroll
+                        for (uint32_t k = 1; k < 4; ++k)
+                            if (k == p.dconv - 1) wl = cwh[k];
+                        acc += __half2float(vh) * __half2float(wl);
+                        const __half o = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
+                        if (dA < p.di) p.xs[(uint64_t)mA * p.di + dA] = o;
+                        else if (dA < p.di + GN) p.Bs[(uint64_t)mA * GN + (dA - p.di)] = o;
+                        else p.Cs[(uint64_t)mA * GN + (dA - p.di - GN)] = o;
+                    }
+                }
+                cons_sync();   // partial sums reused by the next group
+            }
+            stamp(lb + 2);
+            if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
+            stamp(lb + 3);
+            // ---- B: ssd_step + gate over this CTA's state rows
+            {
+                const uint32_t nrows = r1 - r0, mh0 = r0 / p.P;
+                const uint32_t nslot = nrows ? (r1 - 1) / p.P - mh0 + 1 : 0;
+                if (tid < nslot * 32) {   // B / C vectors of each (seq, head) slot
+                    const uint32_t sl = tid >> 5, mh = mh0 + sl, m = mh / p.H, h = mh % p.H, g = h / hpg;
+                    const uint64_t off = (uint64_t)m * GN + g * p.N + lane * 4;
+                    *reinterpret_cast<uint2*>(bcs + sl * 256 + lane * 4) = __ldcg(reinterpret_cast<const uint2*>(p.Bs + off));
+                    *reinterpret_cast<uint2*>(bcs + sl * 256 + 128 + lane * 4) =
+                        __ldcg(reinterpret_cast<const uint2*>(p.Cs + off));
+                } else if (tid >= 128 && tid - 128 < nrows) {   // per-row scalars
+                    const uint32_t j = tid - 128, row = r0 + j;
+                    const uint32_t pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
+                    const float A = -expf(__half2float(L.A_log[h]));
+                    const float dt = fminf(fmaxf(softplus(__half2float(__ldcg(p.projb + (uint64_t)m * p.proj + p.di + p.xd + h)) +
+                                                          __half2float(L.dt_bias[h])), 1e-6f), 1e6f);
+                    const float xv = __half2float(__ldcg(p.xs + (uint64_t)m * p.di + h * p.P + pp));
+                    float* rv = rowv + j * 5;
+                    rv[0] = expf(A * dt);
+                    rv[1] = dt * xv;
+                    rv[2] = __half2float(L.D[h]);
+                    rv[3] = xv;
+                    rv[4] = __half2float(__ldcg(p.projb + (uint64_t)m * p.proj + h * p.P + pp));
+                }
+                if (!mbar_wait_ab(smem_u32(sfull), sphase, abort)) { ok = false; break; }
+                sphase ^= 1;
+                cons_sync();
+                for (uint32_t j0 = warp; j0 < nrows; j0 += 2 * CONS_WARPS) {
+                    float a2[2];
+                    float4 v2[2];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint32_t j = min(j0 + q * CONS_WARPS, nrows - 1);
+                        const uint32_t sl = (r0 + j) / p.P - mh0;
+                        const float* rv = rowv + j * 5;
+                        const uint2 bu = *reinterpret_cast<const uint2*>(bcs + sl * 256 + lane * 4);
+                        const uint2 cu = *reinterpret_cast<const uint2*>(bcs + sl * 256 + 128 + lane * 4);
+                        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bu.x));
+                        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bu.y));
+                        const float2 c01 = __half22float2(*reinterpret_cast<const __half2*>(&cu.x));
+                        const float2 c23 = __half22float2(*reinterpret_cast<const __half2*>(&cu.y));
+                        const float dec = rv[0], dtx = rv[1];
+                        float4 v = *reinterpret_cast<const float4*>(sstate + (uint64_t)j * p.N + lane * 4);
+                        v.x = dec * v.x + b01.x * dtx;
+                        v.y = dec * v.y + b01.y * dtx;
+                        v.z = dec * v.z + b23.x * dtx;
+                        v.w = dec * v.w + b23.y * dtx;
+                        v2[q] = v;
+                        a2[q] = c01.x * v.x + c01.y * v.y + c23.x * v.z + c23.y * v.w;
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        a2[0] += __shfl_xor_sync(0xffffffffu, a2[0], o);
+                        a2[1] += __shfl_xor_sync(0xffffffffu, a2[1], o);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint32_t j = j0 + q * CONS_WARPS;
+                        if (j >= nrows) continue;
+                        const uint32_t row = r0 + j;
+                        *reinterpret_cast<float4*>(L.ssd_state + (uint64_t)row * p.N + lane * 4) = v2[q];
+                        if (lane == 0) {
+                            const float* rv = rowv + j * 5;
+                            const uint32_t pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
+                            const float yh = __half2float(__float2half_rn(a2[q] + rv[2] * rv[3]));
+                            p.gated[(uint64_t)m * p.di + h * p.P + pp] = __float2half_rn(silu(rv[4]) * yh);
+                        }
+                    }
+                }
+            }
+            if (!ok) break;
+            // the state rows written above are read back by a later bulk copy (async proxy)
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            stamp(lb + 4);
+            if (!grid_sync(p, gen, abort)) { ok = false; break; }
+            if (tid == 0) mbar_arrive1(smem_u32(sempty));   // all reads of the state buffer are done
+            stamp(lb + 5);
+            // ---- C: RMSNorm(gated) + out_proj + residual
+            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, p.B, p.di, true, xbuf, red);
+            stamp(lb + 6);
+            for (uint32_t g0 = 0; g0 < ntC && ok; g0 += TG) {
+                const uint32_t nt = min(TG, ntC - g0);
+                if (!consume_group(true, p.seg_out, nchC, p.di, nt)) { ok = false; break; }
+                if (ownC && tiC >= g0 && tiC < g0 + nt && rC < p.dm) {
+                    // block_out rounded to fp16, then hidden += block_out (residual epilogue of k_gemv.cu)
+                    const float o = __half2float(__float2half_rn(reduce_item(tiC - g0, rowC, mC)));
+                    const __half nh = __float2half_rn(hreg + o);
+                    hreg = __half2float(nh);
+                    p.hidden[(uint64_t)mC * p.dm + rC] = nh;
+                }
+                cons_sync();
+            }
+            stamp(lb + 7);
+            if (tr) p.trace[tbase + lb + 9] = wait_ns;
+            if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
+        }
+        if (!ok) break;
+        // ---- lm_head + first-max argmax partials
+        wait_ns = 0;
+        stage_norm(p.hidden, p.dm, nullptr, nullptr, p.norm_f, p.B, p.dm, false, xbuf, red);
+        stamp(lmb + 0);
+        float bv = -INFINITY;
+        uint32_t bi = 0xFFFFFFFFu;
+        for (uint32_t g0 = 0; g0 < ntL && ok; g0 += TG) {
+            const uint32_t nt = min(TG, ntL - g0);
+            if (!consume_group(false, p.seg_lm, nchL, p.dm, nt)) { ok = false; break; }
+            if (tid < nt * 16 * p.B) {
+                const uint32_t ti = tid / (16 * p.B), row = (tid / p.B) % 16, m = tid % p.B;
+                const uint32_t r = (cta + (g0 + ti) * G) * 16 + row;
+                if (r < p.V) {
+                    const __half vh = __float2half_rn(reduce_item(ti, row, m));
+                    p.logits[(uint64_t)m * p.V + r] = vh;
+                    const float f = __half2float(vh);
+                    if (f > bv) { bv = f; bi = r; }        // rows arrive in increasing order per thread
+                }
+            }
+            cons_sync();
+        }
+        if (!ok) break;
+        if (tr) p.trace[tbase + lmb + 4] = wait_ns;
+        // CTA first-max per sequence (thread tid serves sequence tid % B)
+        warp_argmax(bv, bi, p.B);
+        if (lane < p.B) { argv[warp * 2 + lane] = bv; argi[warp * 2 + lane] = bi; }
+        cons_sync();
+        if (tid < p.B) {
+            float v = -INFINITY;
+            uint32_t ix = 0xFFFFFFFFu;
+            for (uint32_t w = 0; w < CONS_WARPS; ++w) argmax_take(v, ix, argv[w * 2 + tid], argi[w * 2 + tid]);
+            p.part_val[(uint64_t)cta * p.B + tid] = v;
+            p.part_idx[(uint64_t)cta * p.B + tid] = ix;
+        }
+        stamp(lmb + 1);
+        if (!grid_sync(p, gen, abort)) { ok = false; break; }
+        stamp(lmb + 2);
+        {
+            // all CTAs' partials in one parallel round of loads (entry e serves sequence e % B)
+            float v = -INFINITY;
+            uint32_t ix = 0xFFFFFFFFu;
+            for (uint32_t e = tid; e < G * p.B; e += CONS)
+                argmax_take(v, ix, __ldcg(p.part_val + e), __ldcg(p.part_idx + e));
+            warp_argmax(v, ix, p.B);
+            if (lane < p.B) { argv[warp * 2 + lane] = v; argi[warp * 2 + lane] = ix; }
+            cons_sync();
+            if (tid < p.B) {
+                const uint32_t m = tid;
+                float bv2 = -INFINITY;
+                uint32_t bi2 = 0xFFFFFFFFu;
+                for (uint32_t w = 0; w < CONS_WARPS; ++w) argmax_take(bv2, bi2, argv[w * 2 + m], argi[w * 2 + m]);
+                const float l0 = __half2float(__ldcg(p.logits + (uint64_t)m * p.V));
+                uint32_t pick = bi2 == 0xFFFFFFFFu ? 0u : bi2;
+                if (l0 != l0) pick = 0;
+                tok[m] = pick;
+                if (cta == 0) {
+                    p.history[(uint64_t)m * p.hist_stride + step] = pick;
+                    p.cur[m] = pick;
+                }
+            }
+            cons_sync();
+        }
+        stamp(lmb + 3);
+    }
+    if (!ok) {
+        *abort = 1;
+        if (tid == 0) atomicExch(p.err, 1);
+    }
+}
+
+// Host launcher: cooperative launch with one CTA per SM (co-residency guaranteed or
+// the launch fails, so the grid barriers cannot wait on a CTA that never runs).
+cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(k_decode_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persist, THREADS, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorNotSupported;
+    PParams p = prm;
+    void* args[] = {&p};
+    return cudaLaunchCooperativeKernel((void*)k_decode_persist, dim3(sm_count), dim3(THREADS), args, SMEM_BYTES, s);
+}
+
+// ---------------------------------------------------------------------------
+//  Host helpers: shape plan and tensor maps
+// ---------------------------------------------------------------------------
+namespace {
+
+// Largest odd segment count <= SEG_MAX that divides `total` segments.
+uint32_t odd_seg(uint32_t total) {
+    for (uint32_t s = SEG_MAX; s >= 1; s -= 2)
+        if (total % s == 0) return s;
+    return 1;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// [rows][segs][128 B] view of a row-major matrix with `row_bytes` per row; box = 16 rows
+// x seg segments, 128-byte swizzle; f16 selects the element type (fp16 rows, or bytes
+// holding INT4 nibble pairs).
+bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t seg, bool f16) {
+    auto enc = encode_tiled();
+    if (!enc) return false;
+    const uint64_t esz = f16 ? 2 : 1;
+    cuuint64_t dims[3] = {128 / esz, row_bytes / 128, rows};
+    cuuint64_t strides[2] = {128, row_bytes};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / esz), seg, 16};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// INT4_B32 scales [rows][K/32] fp16; box = 16 rows x seg*8 scales, no swizzle.
+bool map_scales(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t seg) {
+    auto enc = encode_tiled();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {K / 32, rows};
+    cuuint64_t strides[1] = {K / 16};
+    cuuint32_t box[2] = {seg * 8, 16};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32_t* seg_out, uint32_t* seg_lm) {
+    const uint32_t G = sh.sm_count;
+    if (sh.B < 1 || sh.B > 2) return "batch must be 1 or 2";
+    if (sh.N != 128) return "d_state must be 128";
+    if (sh.P < 32) return "d_head must be >= 32";
+    if (sh.dconv < 1 || sh.dconv > 4) return "d_conv must be 1..4";
+    if (sh.dm % 256 || sh.di % 256) return "d_model and d_inner must be multiples of 256";
+    if (sh.dm / 8 > 3 * CONS || sh.di / 8 > 3 * CONS) return "d_model / d_inner too wide for the staged RMSNorm";
+    if ((uint64_t)sh.B * (sh.dm > sh.di ? sh.dm : sh.di) * 2 > XBUF) return "staged activations exceed 20 KB";
+    if (sh.n_layer > LT_MAX) return "more than 64 layers";
+    if (((sh.proj + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many in_proj rows per SM";
+    if (((sh.dm + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many out_proj rows per SM";
+    if (((uint64_t)sh.B * sh.H * sh.P + G - 1) / G > SROWS) return "ssd state rows per SM exceed 36 KB";
+    *seg_in = odd_seg(sh.dm / 256);
+    *seg_out = odd_seg(sh.di / 256);
+    *seg_lm = odd_seg(sh.dm / 64);
+    return "";
+}
+
+size_t decode_persist_maps_bytes(uint32_t n_layer) { return (size_t)(4 * n_layer + 1) * sizeof(CUtensorMap); }
+
+bool decode_persist_encode_maps(void* out, const PLayer* layers, const void* lm_head, const PersistShape& sh,
+                                uint32_t seg_in, uint32_t seg_out, uint32_t seg_lm) {
+    CUtensorMap* m = static_cast<CUtensorMap*>(out);
+    for (uint32_t l = 0; l < sh.n_layer; ++l) {
+        const uint8_t* in_w = layers[l].in_w;
+        const uint8_t* out_w = layers[l].out_w;
+        if (!map_rows(&m[4 * l + 0], in_w, sh.proj, sh.dm / 2, seg_in, false) ||
+            !map_scales(&m[4 * l + 1], in_w + (size_t)sh.proj * sh.dm / 2, sh.proj, sh.dm, seg_in) ||
+            !map_rows(&m[4 * l + 2], out_w, sh.dm, sh.di / 2, seg_out, false) ||
+            !map_scales(&m[4 * l + 3], out_w + (size_t)sh.dm * sh.di / 2, sh.dm, sh.di, seg_out))
+            return false;
+    }
+    return map_rows(&m[4 * sh.n_layer], lm_head, sh.V, (uint64_t)sh.dm * 2, seg_lm, true);
+}
+
+}  // namespace lssm

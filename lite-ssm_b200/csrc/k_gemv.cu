@@ -16,6 +16,7 @@
 // (store / SiLU / residual add).
 #include "device_util.cuh"
 #include "lssm_internal.h"
+#include "mma_int4.cuh"
 
 namespace lssm {
 
@@ -180,42 +181,6 @@ cudaError_t launch_gemv_f16_f32out(const void* x, const void* w, float* y, uint3
 //  the same permutation (batch rows are the 8 MMA columns), D is the block partial in
 //  fp32, which is multiplied by the block scale and accumulated.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t lop3_6a(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// word -> q pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7) as packed half2 bit patterns.
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t q[4]) {
-    const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u;
-    const uint32_t MLO = 0x64086408u, MHI = 0x64806480u;
-    const __half2 sub_lo = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
-    const __half2 mul_hi = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
-    const __half2 add_hi = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));  // -72
-    uint32_t p0 = lop3_6a(w, LO, MLO);
-    uint32_t p1 = lop3_6a(w, HI, MHI);
-    const uint32_t w8 = w >> 8;
-    uint32_t p2 = lop3_6a(w8, LO, MLO);
-    uint32_t p3 = lop3_6a(w8, HI, MHI);
-    __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&p0), sub_lo);
-    __half2 h1 = __hfma2(*reinterpret_cast<__half2*>(&p1), mul_hi, add_hi);
-    __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&p2), sub_lo);
-    __half2 h3 = __hfma2(*reinterpret_cast<__half2*>(&p3), mul_hi, add_hi);
-    q[0] = *reinterpret_cast<uint32_t*>(&h0);
-    q[1] = *reinterpret_cast<uint32_t*>(&h1);
-    q[2] = *reinterpret_cast<uint32_t*>(&h2);
-    q[3] = *reinterpret_cast<uint32_t*>(&h3);
-}
-
-__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // Stage x (M rows, fp16, optionally RMS-normalised with rr) into shared memory in
 // MMA-fragment order: for row m, block b, quad c the 8 halves x[32b+8c+{0,4,1,5,2,6,3,7}].
 __device__ __forceinline__ void stage_x_frag(const __half* __restrict__ x, const __half* __restrict__ nw,
@@ -332,29 +297,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_int4_mma(const __half* __
 //  register-operand mma.sync dequant as k_gemv_int4_mma, reading words from shared
 //  memory instead of global.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool bar_wait_bounded(uint32_t bar, uint32_t parity) {
-    uint32_t ok = 0;
-    uint64_t t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    while (true) {
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        uint64_t t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (t - t0 > 2000000000ull) return false;
-    }
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_int4_tma(const __half* __restrict__ x,
                                                               const uint8_t* __restrict__ packed,

@@ -107,4 +107,40 @@ struct StepArgs {
 };
 cudaError_t launch_ssd_step_ex(const StepArgs& a, cudaStream_t s);
 
+// ---- persistent decode kernel (k_decode_persist.cu) -------------------------
+struct PLayer {
+    const uint8_t* in_w;       // in_proj packed (proj x dm/2); scales at in_w + proj*dm/2
+    const uint8_t* out_w;      // out_proj packed (dm x di/2); scales at out_w + dm*di/2
+    const __half* conv_w; const __half* conv_b;
+    const __half* dt_bias; const __half* A_log; const __half* D;
+    const __half* norm_w; const __half* mixer_norm_w;
+    __half* conv_state;        // (B, xd, dconv)
+    float* ssd_state;          // (B, H, P, N)
+};
+
+struct PParams {
+    const PLayer* layers; uint32_t n_layer;
+    const __half* embed; const __half* norm_f; const __half* lm_head;
+    __half* hidden; __half* projb; __half* xs; __half* Bs; __half* Cs; __half* gated; __half* logits;
+    float* part_val; uint32_t* part_idx;     // (gridDim, B)
+    uint32_t* cur; uint32_t* history; uint32_t hist_stride; uint32_t n_steps;
+    uint32_t* bar; int* err;
+    uint32_t B, dm, di, xd, proj, H, P, N, G, dconv, V;
+    const void* maps;                        // CUtensorMap[4 * n_layer + 1] in device memory
+    uint32_t seg_in, seg_out, seg_lm;        // 128-byte segments per streamed chunk (odd)
+    // Optional phase trace of the first step: per CTA, TRACE_PER_LAYER %globaltimer
+    // stamps per layer then TRACE_LM stamps for lm_head (null = off).
+    uint64_t* trace;
+};
+constexpr uint32_t TRACE_PER_LAYER = 10, TRACE_LM = 6;
+cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s);
+// Host helpers: the shape limits of the persistent kernel and its tensor maps.
+struct PersistShape { uint32_t n_layer, B, dm, di, xd, proj, H, P, N, G, dconv, V, sm_count; };
+// Returns "" when the kernel can run this shape (and fills the chunk segments), else why not.
+const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32_t* seg_out, uint32_t* seg_lm);
+size_t decode_persist_maps_bytes(uint32_t n_layer);
+// Encodes the 4 * n_layer + 1 tensor maps into host memory `out` (decode_persist_maps_bytes).
+bool decode_persist_encode_maps(void* out, const PLayer* layers, const void* lm_head, const PersistShape& sh,
+                                uint32_t seg_in, uint32_t seg_out, uint32_t seg_lm);
+
 }  // namespace lssm

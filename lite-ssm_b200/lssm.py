@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -121,6 +122,7 @@ _SIGS = {
     "lssm_session_timing": [P, C.POINTER(f32), C.POINTER(f32)],
     "lssm_session_set_option": [P, C.c_char_p, C.c_int64],
     "lssm_session_launches": [P, C.POINTER(u64), C.POINTER(u64)],
+    "lssm_session_trace": [P, C.POINTER(u64), u64, C.POINTER(u64)],
 }
 _OTHER = {
     "lssm_last_error": (C.c_char_p, []),
@@ -187,9 +189,25 @@ class Ctx:
         check(lib().lssm_ctx_create(device, C.byref(h)))
         self.h = h
         self.device = device
+        self._deps = []   # weak refs to sessions / models / buffers made on this context
+
+    def _track(self, obj):
+        if len(self._deps) > 256:
+            self._deps = [r for r in self._deps if r() is not None]
+        self._deps.append(weakref.ref(obj))
 
     def close(self):
+        """Destroys what was made on this context (newest first), then the context, so no
+        native object outlives the context it points to."""
         if self.h:
+            for r in reversed(self._deps):
+                o = r()
+                if o is not None:
+                    try:
+                        (o.close if hasattr(o, "close") else o.free)()
+                    except Exception:
+                        pass
+            self._deps.clear()
             lib().lssm_ctx_destroy(self.h)
             self.h = None
 
@@ -228,6 +246,7 @@ class DeviceBuffer:
         p = P()
         check(lib().lssm_alloc(ctx.h, max(self.nbytes, 1), C.byref(p)))
         self.ptr = p
+        ctx._track(self)
 
     @classmethod
     def from_array(cls, ctx: Ctx, a: np.ndarray, extra: int = 0):
@@ -352,6 +371,7 @@ class Model:
     def __init__(self, ctx: Ctx, handle):
         self.ctx = ctx
         self.h = handle
+        ctx._track(self)
 
     @classmethod
     def load(cls, ctx: Ctx, path: str):
@@ -418,6 +438,7 @@ class Session:
         h = P()
         check(lib().lssm_session_create(ctx.h, model.h, batch, max_seq_len, C.byref(h)))
         self.h = h
+        ctx._track(self)
 
     def reset(self):
         check(lib().lssm_session_reset(self.h))
@@ -459,6 +480,15 @@ class Session:
         a, b = u64(), u64()
         check(lib().lssm_session_launches(self.h, C.byref(a), C.byref(b)))
         return a.value, b.value
+
+    def trace(self) -> np.ndarray:
+        """Phase stamps of the last persistent decode (set_option("trace", 1) first):
+        (sm_count, n_layer * 10 + 6) uint64, layout as lssm_session_trace documents."""
+        n = u64()
+        check(lib().lssm_session_trace(self.h, None, 0, C.byref(n)))
+        out = np.zeros(n.value, dtype=np.uint64)
+        check(lib().lssm_session_trace(self.h, out.ctypes.data_as(C.POINTER(u64)), n.value, C.byref(n)))
+        return out.reshape(-1, self.model.config().n_layer * 10 + 6)
 
     def close(self):
         if self.h:
