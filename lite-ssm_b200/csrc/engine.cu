@@ -504,6 +504,7 @@ struct lssm_session {
     uint32_t* d_bar = nullptr;
     uint32_t seg_in = 0, seg_out = 0, seg_lm = 0;
     void* d_maps = nullptr;        // CUtensorMap[4 * n_layer + 1]
+    float* d_opart = nullptr;      // out_proj partial-sum slots of the persistent kernel
     const char* persist_why = "";  // why the persistent kernel is not used ("" = it is)
     uint64_t* d_trace = nullptr;   // phase stamps of the persistent kernel's first step
     bool trace_on = false;
@@ -522,7 +523,7 @@ extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
     if (s->graph) cudaGraphExecDestroy(s->graph);
     void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
                   s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
-                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps};
+                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart};
     for (void* p : ps)
         if (p) cudaFree(p);
     for (auto& e : s->ev)
@@ -588,6 +589,9 @@ static lssm_status setup_persistent(lssm_session* s) {
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_players), pl.size() * sizeof(PLayer), "session: layer table")))
         return st;
     if ((st = s_alloc(&s->d_maps, maps.size(), "session: tensor maps"))) return st;
+    const size_t nchC = m->d_inner / (s->seg_out * 256);
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_opart), nchC * s->batch * h.d_model * 4, "session: out_proj slots")))
+        return st;
     const size_t parts = (size_t)s->ctx->sm_count * s->batch;
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_val), parts * 4, "session: argmax partials"))) return st;
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_idx), parts * 4, "session: argmax partials"))) return st;
@@ -609,7 +613,7 @@ static PParams persist_params(lssm_session* s, uint32_t n_steps) {
     p.embed = hp(m->embed);
     p.norm_f = hp(m->norm_f);
     p.lm_head = hp(m->lm_head);
-    p.hidden = s->hidden; p.projb = s->proj; p.xs = s->xs; p.Bs = s->Bs; p.Cs = s->Cs;
+    p.projb = s->proj; p.xs = s->xs; p.Bs = s->Bs; p.Cs = s->Cs; p.opart = s->d_opart;
     p.gated = s->gated; p.logits = s->logits;
     p.part_val = s->d_part_val; p.part_idx = s->d_part_idx;
     p.cur = s->d_cur; p.history = s->d_hist; p.hist_stride = s->hist_cap; p.n_steps = n_steps;

@@ -16,26 +16,30 @@
 //     runs ahead across phase boundaries and grid barriers: HBM stays busy while the
 //     consumers synchronise.
 //   * warps 0..6 consume. Each warp releases a ring slot as soon as it has read it;
-//     a CTA's tiles of a phase are accumulated in registers in groups of up to 5 and
-//     reduced across warps once per group. Per layer:
-//       A  RMSNorm(hidden) staged in MMA-fragment order, in_proj INT4 GEMV on
-//          register-operand mma.sync (the dequantisation of k_gemv.cu), epilogue:
-//          z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
-//          (each epilogue thread loaded its conv weights / state at layer start)
+//     tiles / units are accumulated in registers in groups of up to 5 and reduced
+//     across warps once per group. Per layer:
+//       A  residual (hidden += half(sum of out_proj slots); every SM keeps the whole
+//          hidden vector in shared memory) + RMSNorm, staged in MMA-fragment order;
+//          in_proj INT4 GEMV tiles (16 rows x all of K) on register-operand mma.sync
+//          (the dequantisation of k_gemv.cu); epilogue: z / dt stored, xBC rows ->
+//          conv-state roll + conv + SiLU -> x, B, C (each epilogue thread loaded its
+//          conv weights / state at layer start)
 //       -- grid barrier --
-//       B  ssd_step + gate on the CTA's state rows (already in shared memory), with
+//       B  ssd_step + gate on the SM's state rows (already in shared memory), with the
 //          B / C vectors and per-row scalars staged in one parallel round of loads:
 //          S = e^{A dt} S + dt B x, y = C.S + D x, gated = half(silu(z) * half(y))
 //       -- grid barrier --
-//       C  RMSNorm(gated) staged, out_proj INT4 GEMV, residual add into hidden (each
-//          epilogue thread keeps its hidden element in a register across layers)
+//       C  RMSNorm(gated) staged; out_proj work cut into (16-row tile, K chunk) units
+//          dealt round-robin over the SMs (every SM gets the same number +-1); each
+//          unit's fp32 partial sums go to their own slot, and the next RMSNorm adds
+//          the slots in a fixed order (deterministic, no atomics)
 //       -- grid barrier --
-//     then norm_f + lm_head (fp16 weights, mma.sync), per-CTA first-max argmax
-//     partials, a grid barrier, and every CTA reduces the partials to the same next
-//     token (no host round-trip; the next token's embedding row is read directly).
-// The tile -> CTA assignment (tile t to CTA t mod grid) is the same in every layer
-// and step, so the rows a CTA owns (conv state, ssd state, hidden) are only ever
-// written by that CTA.
+//     then residual + norm_f + lm_head (fp16 weights, mma.sync), per-CTA first-max
+//     argmax partials, a grid barrier, and every CTA reduces the partials to the
+//     same next token (no host round-trip; the next token's embedding row is read
+//     directly).
+// The row -> SM assignments are the same in every layer and step, so each conv-state
+// and ssd-state row is only ever written by its owner SM.
 // Grid barriers are a monotonically increasing global counter (release add, acquire
 // spin) with a 2 s %globaltimer bound; every mbarrier wait is bounded too. A timeout
 // sets the error word and all CTAs leave after draining their in-flight copies.
@@ -64,15 +68,19 @@ constexpr uint32_t XBUF = 20480;                          // staged activation (
 constexpr uint32_t PART = TG * CONS_WARPS * 32 * 4 * 4;   // per-warp partial sums of one group
 constexpr uint32_t SBUF = 36864;                          // this CTA's ssd state rows (<= 72 x 128 fp32)
 constexpr uint32_t SROWS = SBUF / 512;
-constexpr uint32_t BSLOTS = 4;                            // (seq, head) B / C vector slots in phase B
+constexpr uint32_t HBUF = 10240;                          // hidden vector(s) (B x d_model fp16)
+constexpr uint32_t BSLOTS = 4;                            // (seq, group) B / C vector slots in phase B
+constexpr uint32_t NCH_MAX = 4;                           // out_proj K chunks (partial slots)
 constexpr uint32_t LT_MAX = 64;                           // layers whose table entries fit in smem
 constexpr uint32_t OFF_RING = 0;
 constexpr uint32_t OFF_X = OFF_RING + RING * STAGE;
 constexpr uint32_t OFF_PART = OFF_X + XBUF;
 constexpr uint32_t OFF_S = OFF_PART + PART;
-constexpr uint32_t OFF_BC = OFF_S + SBUF;                 // BSLOTS x {B, C} x 128 halves
+constexpr uint32_t OFF_H = OFF_S + SBUF;
+constexpr uint32_t OFF_BC = OFF_H + HBUF;                 // BSLOTS x {B, C} x 128 halves
 constexpr uint32_t OFF_ROWV = OFF_BC + BSLOTS * 512;      // SROWS x 5 floats
-constexpr uint32_t OFF_LT = OFF_ROWV + SROWS * 5 * 4;     // layer table
+constexpr uint32_t OFF_RSLOT = OFF_ROWV + SROWS * 5 * 4;  // SROWS slot ids + BSLOTS (seq, group) keys
+constexpr uint32_t OFF_LT = OFF_RSLOT + 128;              // layer table
 constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[16], tok[2], abort, arg v[16] / i[16]
@@ -177,15 +185,19 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
 }
 
 // INT4 chunk (16 rows x seg*256 k): this warp's share of the chunk's 32-wide blocks.
-// x is staged over the whole K in fragment order (4 uint4 per 32-k block).
+// x is staged over the whole K in fragment order (4 uint4 per 32-k block). Rows g and
+// g + 8 share the swizzle phase (8 * seg lines apart), so one offset serves both.
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
                                              uint32_t K8, uint32_t M, float acc[4]) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, c = lane & 3;
-    const uint32_t nb = seg * 8;
-    const __half* sc = reinterpret_cast<const __half*>(stage + 16 * seg * 128);
+    const uint32_t nb = seg * 8, rowb = seg * 128;
+    const uint8_t* ra = stage + g * rowb + 4 * c;
+    const uint8_t* rb = ra + 8 * rowb;
+    const uint32_t sw = (g * seg) & 7;
+    const __half* sc = reinterpret_cast<const __half*>(stage + 16 * rowb);
     const __half* sa = sc + g * nb;
-    const __half* sbp = sc + (g + 8) * nb;
+    const __half* sbp = sa + 8 * nb;
     const bool has_x = g < M;
     const uint4* xrow = xs + (uint64_t)(has_x ? g : 0) * K8 + (uint64_t)chunk * nb * 4 + c;
     const uint32_t b0 = (nb * warp) / CONS_WARPS, b1 = (nb * (warp + 1)) / CONS_WARPS;
@@ -196,10 +208,11 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
     for (uint32_t i = 0; i < MAXB; ++i) {
         const uint32_t b = b0 + i;
         if (b >= b1) break;
-        const uint32_t s = b >> 3, j = b & 7;
+        const uint32_t s = b >> 3;
+        const uint32_t off = (s << 7) + (((b & 7) ^ ((sw + s) & 7)) << 4);
         const uint4 xf = has_x ? xrow[b * 4] : make_uint4(0, 0, 0, 0);
-        const uint32_t wa = *reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j) + 4 * c);
-        const uint32_t wb = *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j) + 4 * c);
+        const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
+        const uint32_t wb = *reinterpret_cast<const uint32_t*>(rb + off);
         uint32_t qa[4], qb[4];
         dequant_word(wa, qa);
         dequant_word(wb, qb);
@@ -318,6 +331,108 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
     cons_sync();
 }
 
+// RMSNorm input of in_proj / lm_head, with the previous layer's residual folded in:
+// per sequence m, hidden[k] = half(hidden[k] + half(sum_c opart[c][m][k])) (the out_proj
+// output rounded to fp16, then hidden += block_out, mamba2_block.cpp:274-276), or
+// hidden = embed[tok[m]] at layer 0. `hid` (shared memory) keeps the updated vector for
+// the next layer; the normalised fp16 values go to xbuf as in stage_norm. Every SM
+// computes the same vector (same inputs, same order of additions). The residual pass
+// works on 4-element quads (<= 3 per thread: K <= 2688), all slot loads in flight at once.
+__device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* tok, const __half* embed, __half* hid,
+                             const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* red) {
+    const uint32_t tid = threadIdx.x, nq = K / 8, n4 = K / 4;
+    uint4 wv[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const uint32_t q = tid + i * CONS;
+        if (q < nq) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + q);
+    }
+    for (uint32_t m = 0; m < M; ++m) {
+        __half* hrow = hid + (uint64_t)m * K;
+        uint2 hv[3];
+        float4 o[3];
+        // slots summed two at a time (c = 0, 1 then 2, 3): the same fixed order, and at
+        // most 6 float4 loads in flight per thread
+#pragma unroll
+        for (uint32_t c0 = 0; c0 < NCH_MAX; c0 += 2) {
+            if (tok || c0 >= nch) break;
+            float4 pa[3][2];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const uint32_t q = tid + i * CONS;
+                if (q >= n4) continue;
+#pragma unroll
+                for (uint32_t c = 0; c < 2; ++c)
+                    if (c0 + c < nch)
+                        pa[i][c] = __ldcg(reinterpret_cast<const float4*>(opart + ((uint64_t)(c0 + c) * M + m) * K) + q);
+            }
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const uint32_t q = tid + i * CONS;
+                if (q >= n4) continue;
+#pragma unroll
+                for (uint32_t c = 0; c < 2; ++c) {
+                    if (c0 + c >= nch) continue;
+                    if (c0 + c == 0) o[i] = pa[i][0];
+                    else { o[i].x += pa[i][c].x; o[i].y += pa[i][c].y; o[i].z += pa[i][c].z; o[i].w += pa[i][c].w; }
+                }
+            }
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint32_t q = tid + i * CONS;
+            if (q >= n4) continue;
+            hv[i] = tok ? __ldcg(reinterpret_cast<const uint2*>(embed + (uint64_t)tok[m] * K) + q)
+                        : reinterpret_cast<const uint2*>(hrow)[q];
+            __half* h4 = reinterpret_cast<__half*>(&hv[i]);
+            if (!tok) {
+                const float ov[4] = {o[i].x, o[i].y, o[i].z, o[i].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    h4[j] = __float2half_rn(__half2float(h4[j]) + __half2float(__float2half_rn(ov[j])));
+            }
+            reinterpret_cast<uint2*>(hrow)[q] = hv[i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float f = __half2float(h4[j]);
+                ss += f * f;
+            }
+        }
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        cons_sync();   // also publishes hrow
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CONS_WARPS; ++i) tot += red[i];
+        const float rr = rsqrtf(tot / (float)K + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const uint32_t q = tid + i * CONS;
+            if (q >= nq) continue;
+            const uint4 xv = reinterpret_cast<const uint4*>(hrow)[q];
+            const __half* xh8 = reinterpret_cast<const __half*>(&xv);
+            const __half* wh8 = reinterpret_cast<const __half*>(&wv[i]);
+            __half v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(xh8[j]) * __half2float(wh8[j]) * rr);
+            uint4 u;
+            if (frag) {
+                __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
+                __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
+                u.x = *reinterpret_cast<uint32_t*>(&o0);
+                u.y = *reinterpret_cast<uint32_t*>(&o1);
+                u.z = *reinterpret_cast<uint32_t*>(&o2);
+                u.w = *reinterpret_cast<uint32_t*>(&o3);
+            } else {
+                u = *reinterpret_cast<uint4*>(v);
+            }
+            reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
+        }
+        cons_sync();
+    }
+}
+
 // First-max argmax step: (v, i) replaces (bv, bi) when larger, or equal with a lower index.
 __device__ __forceinline__ void argmax_take(float& bv, uint32_t& bi, float v, uint32_t i) {
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -342,34 +457,41 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     float* red = reinterpret_cast<float*>(smem + OFF_MISC);              // 2 x 8 floats
     uint32_t* tok = reinterpret_cast<uint32_t*>(red + 16);                 // 2 tokens
     volatile int* abort = reinterpret_cast<volatile int*>(tok + 2);
+    uint32_t* nslot_s = reinterpret_cast<uint32_t*>(tok + 3);
     float* argv = reinterpret_cast<float*>(smem + OFF_MISC + 128);         // 16 floats
     uint32_t* argi = reinterpret_cast<uint32_t*>(argv + 16);              // 16 ids
     PLayer* LT = reinterpret_cast<PLayer*>(smem + OFF_LT);
     float* part = reinterpret_cast<float*>(smem + OFF_PART);
     uint8_t* xbuf = smem + OFF_X;
     const float* sstate = reinterpret_cast<const float*>(smem + OFF_S);
+    __half* hid = reinterpret_cast<__half*>(smem + OFF_H);
     __half* bcs = reinterpret_cast<__half*>(smem + OFF_BC);
     float* rowv = reinterpret_cast<float*>(smem + OFF_ROWV);
+    uint8_t* rslot = smem + OFF_RSLOT;                                     // per state row: B / C slot
+    uint32_t* skey = reinterpret_cast<uint32_t*>(smem + OFF_RSLOT + 96);  // per slot: m * G + g
     const CUtensorMap* maps = static_cast<const CUtensorMap*>(p.maps);
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
     const uint32_t nA = (p.proj + 15) / 16, nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
-    const uint32_t ntA = cta < nA ? (nA - 1 - cta) / G + 1 : 0;   // this CTA's tiles per phase
-    const uint32_t ntC = cta < nC ? (nC - 1 - cta) / G + 1 : 0;
-    const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;
+    const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
+    const uint32_t uC = nC * nchC;                                  // out_proj (tile, chunk) units
+    const uint32_t ntA = cta < nA ? (nA - 1 - cta) / G + 1 : 0;    // this CTA's in_proj tiles
+    const uint32_t nuC = cta < uC ? (uC - 1 - cta) / G + 1 : 0;    // this CTA's out_proj units
+    const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;    // lm_head tiles
     const uint32_t srows = p.B * p.H * p.P;
     const uint32_t r0 = (uint32_t)(((uint64_t)srows * cta) / G), r1 = (uint32_t)(((uint64_t)srows * (cta + 1)) / G);
-    const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
+    const uint32_t nrows = r1 - r0;
+    const uint32_t GN = p.G * p.N, hpg = p.H / p.G;
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
-    if (((nA + G - 1) / G) * 16 * p.B > CONS || ((nC + G - 1) / G) * 16 * p.B > CONS || p.dconv > 4 || p.dconv < 1 ||
-        p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || (srows + G - 1) / G > SROWS || p.n_layer > LT_MAX ||
-        (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || p.dm / 8 > 3 * CONS || p.di / 8 > 3 * CONS ||
-        p.seg_in > SEG_MAX || p.seg_out > SEG_MAX || p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) ||
-        !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm || nchC * p.seg_out * 256 != p.di ||
-        nchL * p.seg_lm * 64 != p.dm) {
+    if (p.dconv > 4 || p.dconv < 1 || p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || (srows + G - 1) / G > SROWS ||
+        p.n_layer > LT_MAX || (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || (uint64_t)p.B * p.dm * 2 > HBUF ||
+        p.dm / 8 > 3 * CONS || p.di / 8 > 3 * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
+        p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
+        nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
+        p.H % p.G || ((nA + G - 1) / G) * 16 * p.B > CONS || p.dm / 4 > 3 * CONS) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -382,12 +504,27 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         mbar_init1(smem_u32(sfull), 1);
         mbar_init1(smem_u32(sempty), 1);
         *abort = 0;
+        // distinct (seq, group) pairs of this CTA's state rows -> B / C slots
+        uint32_t ns = 0;
+        for (uint32_t j = 0; j < nrows; ++j) {
+            const uint32_t mh = (r0 + j) / p.P, key = (mh / p.H) * p.G + (mh % p.H) / hpg;
+            uint32_t sl = 0;
+            while (sl < ns && skey[sl] != key) ++sl;
+            if (sl == ns) {
+                if (ns == BSLOTS) { atomicExch(p.err, 1); *abort = 1; break; }
+                skey[ns++] = key;
+            }
+            rslot[j] = (uint8_t)sl;
+        }
+        *nslot_s = ns;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (tid < p.B) tok[tid] = p.cur[tid];
     for (uint32_t i = tid; i < p.n_layer * (uint32_t)(sizeof(PLayer) / 8); i += THREADS)
         reinterpret_cast<uint64_t*>(LT)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
     __syncthreads();
+    if (*abort) return;
+    const uint32_t nslot = *nslot_s;
 
     const uint64_t tbase = (uint64_t)cta * (p.n_layer * TRACE_PER_LAYER + TRACE_LM);
     const uint32_t lmb = p.n_layer * TRACE_PER_LAYER;
@@ -400,7 +537,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             int last_phase[RING];
             for (int s = 0; s < RING; ++s) last_phase[s] = -1;
             bool state_issued = false;
-            auto take = [&]() -> uint32_t {   // next free stage (bounded wait); ~0u on abort
+            // next free stage (bounded wait); ~0u on abort
+            auto take = [&]() -> uint32_t {
                 if (!mbar_wait_ab(smem_u32(&empty[slot]), phase ^ 1, abort)) return ~0u;
                 return slot;
             };
@@ -408,21 +546,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 last_phase[slot] = (int)phase;
                 if (++slot == RING) { slot = 0; phase ^= 1; }
             };
-            const uint32_t sbytes = (r1 - r0) * p.N * 4;
+            // one INT4 (tile, chunk) unit: weights (3-D, swizzled) + scales (2-D)
+            auto put_int4 = [&](const CUtensorMap* mw, uint32_t seg, uint32_t u, uint32_t nch) -> bool {
+                const uint32_t s = take();
+                if (s == ~0u) return false;
+                const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
+                const int32_t row0 = (int32_t)((u / nch) * 16), c = (int32_t)(u % nch);
+                mbar_expect(bar, 16 * seg * (128 + 16));
+                tma3(dst, mw, 0, c * (int32_t)seg, row0, bar, pol);
+                tma2(dst + 16 * seg * 128, mw + 1, c * (int32_t)seg * 8, row0, bar, pol);
+                advance();
+                return true;
+            };
+            const uint32_t sbytes = nrows * p.N * 4;
             bool ok = true;
             for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
                 for (uint32_t l = 0; l < p.n_layer && ok; ++l) {
                     const CUtensorMap* mp = maps + 4 * l;
                     for (uint32_t ti = 0; ti < ntA && ok; ++ti)
                         for (uint32_t c = 0; c < nchA && ok; ++c) {
-                            const uint32_t s = take();
-                            if (s == ~0u) { ok = false; break; }
-                            const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
-                            const int32_t row0 = (int32_t)((cta + ti * G) * 16);
-                            mbar_expect(bar, 16 * p.seg_in * (128 + 16));
-                            tma3(dst, mp + 0, 0, (int32_t)(c * p.seg_in), row0, bar, pol);
-                            tma2(dst + 16 * p.seg_in * 128, mp + 1, (int32_t)(c * p.seg_in * 8), row0, bar, pol);
-                            advance();
+                            ok = put_int4(mp, p.seg_in, (cta + ti * G) * nchA + c, nchA);
                             if (p.trace && step == 0 && ti == 0 && c == 0)
                                 p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
                         }
@@ -437,17 +580,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     }
                     state_issued = true;
                     sphase ^= 1;
-                    for (uint32_t ti = 0; ti < ntC && ok; ++ti)
-                        for (uint32_t c = 0; c < nchC && ok; ++c) {
-                            const uint32_t s = take();
-                            if (s == ~0u) { ok = false; break; }
-                            const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
-                            const int32_t row0 = (int32_t)((cta + ti * G) * 16);
-                            mbar_expect(bar, 16 * p.seg_out * (128 + 16));
-                            tma3(dst, mp + 2, 0, (int32_t)(c * p.seg_out), row0, bar, pol);
-                            tma2(dst + 16 * p.seg_out * 128, mp + 3, (int32_t)(c * p.seg_out * 8), row0, bar, pol);
-                            advance();
-                        }
+                    for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, p.seg_out, cta + i * G, nchC);
                 }
                 const CUtensorMap* ml = maps + 4 * p.n_layer;
                 for (uint32_t ti = 0; ti < ntL && ok; ++ti)
@@ -473,16 +606,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     uint32_t slot = 0, phase = 0, gen = 0, sphase = 0;
     uint64_t wait_ns = 0;   // trace: warp 0's time blocked on the ring in this layer
 
-    // Consume `nt` (<= TG) consecutive tiles of this CTA: all their chunks, accumulated
-    // per tile in registers; then every warp's partial sums go to shared memory
-    // (readable after the closing barrier).
-    auto consume_group = [&](bool int4, uint32_t seg, uint32_t nch, uint32_t K, uint32_t nt) -> bool {
+    // Consume `nt` (<= TG) units of this CTA starting at unit ordinal i0: units are
+    // (tile, chunk) pairs when `split` (one chunk each), else whole tiles of `nch`
+    // chunks. Accumulated per unit in registers; every warp's partial sums then go to
+    // shared memory (readable after the closing barrier).
+    auto consume_group = [&](bool int4, uint32_t seg, uint32_t nch, uint32_t K, bool split, uint32_t i0,
+                             uint32_t nt) -> bool {
         float acc[TG][4];
 #pragma unroll
         for (uint32_t ti = 0; ti < TG; ++ti) {
             acc[ti][0] = acc[ti][1] = acc[ti][2] = acc[ti][3] = 0.0f;
             if (ti < nt) {
-                for (uint32_t c = 0; c < nch; ++c) {
+                const uint32_t u = cta + (i0 + ti) * G;
+                const uint32_t c0 = split ? u % nch : 0, c1 = split ? c0 + 1 : nch;
+                for (uint32_t c = c0; c < c1; ++c) {
                     const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
                     if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) return false;
                     if (p.trace && tid == 0) wait_ns += gtimer() - w0;
@@ -503,7 +640,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         cons_sync();
         return true;
     };
-    // Cross-warp sum of output (tile ordinal ti within the group, row, m): the m16n8
+    // Cross-warp sum of output (unit ordinal ti within the group, row, m): the m16n8
     // accumulator of lane (g, c) holds rows g / g + 8 and columns (sequences) 2c, 2c + 1.
     auto reduce_item = [&](uint32_t ti, uint32_t row, uint32_t m) -> float {
         const uint32_t src = (row & 7) * 4 + (m >> 1), idx = (m & 1) + ((row >> 3) << 1);
@@ -512,19 +649,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         for (int w = 0; w < CONS_WARPS; ++w) s += part[((ti * CONS_WARPS + w) * 32 + src) * 4 + idx];
         return s;
     };
-
-    // Each thread owns one (tile ordinal, row, seq) output of in_proj and of out_proj.
+    // All units of a split-K GEMV phase: groups of TG units -> partial-sum slots
+    // slots[(chunk * B + m) * N + row].
+    auto gemv_phase = [&](uint32_t seg, uint32_t nch, uint32_t K, uint32_t N, uint32_t nu, float* slots) -> bool {
+        for (uint32_t i0 = 0; i0 < nu; i0 += TG) {
+            const uint32_t nt = min(TG, nu - i0);
+            if (!consume_group(true, seg, nch, K, true, i0, nt)) return false;
+            if (tid < nt * 16 * p.B) {
+                const uint32_t ti = tid / (16 * p.B), row = (tid / p.B) % 16, m = tid % p.B;
+                const uint32_t u = cta + (i0 + ti) * G, r = (u / nch) * 16 + row;
+                if (r < N) slots[((uint64_t)(u % nch) * p.B + m) * N + r] = reduce_item(ti, row, m);
+            }
+            cons_sync();   // partial sums reused by the next group
+        }
+        return true;
+    };
+    // Each thread owns one (tile ordinal, row, seq) output of in_proj for the epilogue.
     const uint32_t tiA = tid / (16 * p.B), rowA = (tid / p.B) % 16, mA = tid % p.B;
     const bool ownA = tiA < ntA;
     const uint32_t rA = (cta + tiA * G) * 16 + rowA;           // in_proj output row
     const bool convA = ownA && rA >= p.di && rA < p.di + p.xd;
     const uint32_t dA = rA - p.di;
-    const uint32_t tiC = tid / (16 * p.B), rowC = (tid / p.B) % 16, mC = tid % p.B;
-    const bool ownC = tiC < ntC;
-    const uint32_t rC = (cta + tiC * G) * 16 + rowC;           // out_proj output row (hidden index)
-    float hreg = 0.0f;                                         // hidden[mC][rC], carried across layers
 
-    const uint32_t GN = p.G * p.N, hpg = p.H / p.G;
     bool ok = true;
     for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
         const bool tr = p.trace && step == 0 && tid == 0;
@@ -536,8 +682,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             const uint32_t lb = l * TRACE_PER_LAYER;
             stamp(lb + 0);
             wait_ns = 0;
-            // ---- loads consumed only in this layer's epilogues (issued first, waited late)
-            // (kept as raw fp16 bits until the epilogue so no conversion waits on them)
+            // ---- loads consumed only in this layer's in_proj epilogue (issued first, waited
+            // late; kept as raw fp16 bits so no conversion waits on them)
             __half cwh[4], csh[4], cbh = __ushort_as_half(0);
 #pragma unroll
             for (uint32_t k = 0; k < 4; ++k) cwh[k] = csh[k] = __ushort_as_half(0);
@@ -549,15 +695,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     if (k < p.dconv) { cwh[k] = wrow[k]; csh[k] = srow[k]; }
                 cbh = L.conv_b[dA];
             }
-            __half h0 = __ushort_as_half(0);
-            if (l == 0 && ownC && rC < p.dm) h0 = p.embed[(uint64_t)tok[mC] * p.dm + rC];
-            if (l == 0) hreg = __half2float(h0);
-            // ---- A: RMSNorm + in_proj + conv/SiLU/split
-            stage_norm(p.hidden, p.dm, l == 0 ? tok : nullptr, p.embed, L.norm_w, p.B, p.dm, true, xbuf, red);
+            // ---- A: residual + RMSNorm, in_proj tiles (all K chunks of a tile), epilogue:
+            // z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
+            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.B, p.dm, true, xbuf, red);
             stamp(lb + 1);
             for (uint32_t g0 = 0; g0 < ntA && ok; g0 += TG) {
                 const uint32_t nt = min(TG, ntA - g0);
-                if (!consume_group(true, p.seg_in, nchA, p.dm, nt)) { ok = false; break; }
+                if (!consume_group(true, p.seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
                 if (ownA && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
                     const __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
                     if (!convA) {
@@ -589,24 +733,22 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             stamp(lb + 2);
             if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
             stamp(lb + 3);
-            // ---- B: ssd_step + gate over this CTA's state rows
+            // ---- B: ssd_step + gate over this CTA's state rows: B / C vectors of its
+            // (seq, group) slots and per-row scalars staged in one parallel round of loads
             {
-                const uint32_t nrows = r1 - r0, mh0 = r0 / p.P;
-                const uint32_t nslot = nrows ? (r1 - 1) / p.P - mh0 + 1 : 0;
-                if (tid < nslot * 32) {   // B / C vectors of each (seq, head) slot
-                    const uint32_t sl = tid >> 5, mh = mh0 + sl, m = mh / p.H, h = mh % p.H, g = h / hpg;
-                    const uint64_t off = (uint64_t)m * GN + g * p.N + lane * 4;
-                    *reinterpret_cast<uint2*>(bcs + sl * 256 + lane * 4) = __ldcg(reinterpret_cast<const uint2*>(p.Bs + off));
-                    *reinterpret_cast<uint2*>(bcs + sl * 256 + 128 + lane * 4) =
-                        __ldcg(reinterpret_cast<const uint2*>(p.Cs + off));
-                } else if (tid >= 128 && tid - 128 < nrows) {   // per-row scalars
-                    const uint32_t j = tid - 128, row = r0 + j;
-                    const uint32_t pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
+                if (tid < nslot * 64) {
+                    const uint32_t sl = tid >> 6, w = tid & 63, key = skey[sl], m = key / p.G, g = key % p.G;
+                    const __half* src = (w < 32 ? p.Bs : p.Cs) + (uint64_t)m * GN + g * p.N + (w & 31) * 4;
+                    *reinterpret_cast<uint2*>(bcs + sl * 256 + (w < 32 ? 0 : 128) + (w & 31) * 4) =
+                        __ldcg(reinterpret_cast<const uint2*>(src));
+                }
+                if (tid < nrows) {
+                    const uint32_t row = r0 + tid, pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
                     const float A = -expf(__half2float(L.A_log[h]));
                     const float dt = fminf(fmaxf(softplus(__half2float(__ldcg(p.projb + (uint64_t)m * p.proj + p.di + p.xd + h)) +
                                                           __half2float(L.dt_bias[h])), 1e-6f), 1e6f);
                     const float xv = __half2float(__ldcg(p.xs + (uint64_t)m * p.di + h * p.P + pp));
-                    float* rv = rowv + j * 5;
+                    float* rv = rowv + tid * 5;
                     rv[0] = expf(A * dt);
                     rv[1] = dt * xv;
                     rv[2] = __half2float(L.D[h]);
@@ -622,10 +764,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const uint32_t j = min(j0 + q * CONS_WARPS, nrows - 1);
-                        const uint32_t sl = (r0 + j) / p.P - mh0;
+                        const __half* bv = bcs + rslot[j] * 256;
                         const float* rv = rowv + j * 5;
-                        const uint2 bu = *reinterpret_cast<const uint2*>(bcs + sl * 256 + lane * 4);
-                        const uint2 cu = *reinterpret_cast<const uint2*>(bcs + sl * 256 + 128 + lane * 4);
+                        const uint2 bu = *reinterpret_cast<const uint2*>(bv + lane * 4);
+                        const uint2 cu = *reinterpret_cast<const uint2*>(bv + 128 + lane * 4);
                         const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bu.x));
                         const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bu.y));
                         const float2 c01 = __half22float2(*reinterpret_cast<const __half2*>(&cu.x));
@@ -666,35 +808,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             if (!grid_sync(p, gen, abort)) { ok = false; break; }
             if (tid == 0) mbar_arrive1(smem_u32(sempty));   // all reads of the state buffer are done
             stamp(lb + 5);
-            // ---- C: RMSNorm(gated) + out_proj + residual
+            // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
             stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, p.B, p.di, true, xbuf, red);
             stamp(lb + 6);
-            for (uint32_t g0 = 0; g0 < ntC && ok; g0 += TG) {
-                const uint32_t nt = min(TG, ntC - g0);
-                if (!consume_group(true, p.seg_out, nchC, p.di, nt)) { ok = false; break; }
-                if (ownC && tiC >= g0 && tiC < g0 + nt && rC < p.dm) {
-                    // block_out rounded to fp16, then hidden += block_out (residual epilogue of k_gemv.cu)
-                    const float o = __half2float(__float2half_rn(reduce_item(tiC - g0, rowC, mC)));
-                    const __half nh = __float2half_rn(hreg + o);
-                    hreg = __half2float(nh);
-                    p.hidden[(uint64_t)mC * p.dm + rC] = nh;
-                }
-                cons_sync();
-            }
+            if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
             if (tr) p.trace[tbase + lb + 9] = wait_ns;
-            if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
+            if (!grid_sync(p, gen, abort)) { ok = false; break; }
         }
         if (!ok) break;
-        // ---- lm_head + first-max argmax partials
+        // ---- residual + norm_f + lm_head + first-max argmax partials
         wait_ns = 0;
-        stage_norm(p.hidden, p.dm, nullptr, nullptr, p.norm_f, p.B, p.dm, false, xbuf, red);
+        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.B, p.dm, false, xbuf, red);
         stamp(lmb + 0);
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
         for (uint32_t g0 = 0; g0 < ntL && ok; g0 += TG) {
             const uint32_t nt = min(TG, ntL - g0);
-            if (!consume_group(false, p.seg_lm, nchL, p.dm, nt)) { ok = false; break; }
+            if (!consume_group(false, p.seg_lm, nchL, p.dm, false, g0, nt)) { ok = false; break; }
             if (tid < nt * 16 * p.B) {
                 const uint32_t ti = tid / (16 * p.B), row = (tid / p.B) % 16, m = tid % p.B;
                 const uint32_t r = (cta + (g0 + ti) * G) * 16 + row;
@@ -837,12 +968,15 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     if (sh.dm / 8 > 3 * CONS || sh.di / 8 > 3 * CONS) return "d_model / d_inner too wide for the staged RMSNorm";
     if ((uint64_t)sh.B * (sh.dm > sh.di ? sh.dm : sh.di) * 2 > XBUF) return "staged activations exceed 20 KB";
     if (sh.n_layer > LT_MAX) return "more than 64 layers";
+    if ((uint64_t)sh.B * sh.dm * 2 > HBUF) return "hidden vectors exceed 10 KB";
     if (((sh.proj + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many in_proj rows per SM";
-    if (((sh.dm + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many out_proj rows per SM";
+    if (sh.dm / 4 > 3 * CONS) return "d_model too wide for the residual pass (<= 2688)";
+    if (sh.H % sh.G) return "n_heads not divisible by n_groups";
     if (((uint64_t)sh.B * sh.H * sh.P + G - 1) / G > SROWS) return "ssd state rows per SM exceed 36 KB";
     *seg_in = odd_seg(sh.dm / 256);
     *seg_out = odd_seg(sh.di / 256);
     *seg_lm = odd_seg(sh.dm / 64);
+    if (sh.di / 256 / *seg_out > NCH_MAX) return "too many out_proj K chunks per row";
     return "";
 }
 

@@ -121,7 +121,9 @@ struct PLayer {
 struct PParams {
     const PLayer* layers; uint32_t n_layer;
     const __half* embed; const __half* norm_f; const __half* lm_head;
-    __half* hidden; __half* projb; __half* xs; __half* Bs; __half* Cs; __half* gated; __half* logits;
+    __half* projb; __half* xs; __half* Bs; __half* Cs;   // in_proj outputs: [z | . | dt], x, B, C (fp16)
+    float* opart;                            // out_proj partial sums [chunk][seq][d_model] fp32
+    __half* gated; __half* logits;
     float* part_val; uint32_t* part_idx;     // (gridDim, B)
     uint32_t* cur; uint32_t* history; uint32_t hist_stride; uint32_t n_steps;
     uint32_t* bar; int* err;
