@@ -60,9 +60,31 @@ def build(verbose: bool = False, extra=()) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_cpp_shim(verbose)
     if verbose:
         print(LIB)
     return LIB
+
+
+SHIM_SRC = HERE / "cpp" / "metal_ops.cpp"
+SHIM_LIB = HERE / "liblite_ssm_ops.so"
+
+
+def build_cpp_shim(verbose: bool = False) -> Path:
+    """liblite_ssm_ops.so: the C++ `lite_ssm::MetalOps` class (include/lite_ssm_b200/ops.hpp)
+    over the C ABI, linked against liblssm_cuda.so next to it (rpath $ORIGIN)."""
+    hdr = ROOT / "include" / "lite_ssm_b200" / "ops.hpp"
+    newest = max(SHIM_SRC.stat().st_mtime, hdr.stat().st_mtime, LIB.stat().st_mtime)
+    if SHIM_LIB.exists() and SHIM_LIB.stat().st_mtime >= newest:
+        return SHIM_LIB
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared", f"-I{ROOT / 'include'}",
+           "-o", str(SHIM_LIB), str(SHIM_SRC), f"-L{HERE}", "-llssm_cuda", "-Wl,-rpath,$ORIGIN", "-ldl"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"C++ shim build failed:\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(SHIM_LIB)
+    return SHIM_LIB
 
 
 if __name__ == "__main__":

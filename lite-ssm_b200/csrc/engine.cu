@@ -825,13 +825,9 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
 static lssm_status logits_of(lssm_session* s, const __half* x, cudaStream_t st) {
     lssm_model* m = s->m;
     const SsmHeader& h = m->img.hdr;
-    for (uint32_t b0 = 0; b0 < s->batch; b0 += 8) {
-        const uint32_t r = std::min<uint32_t>(8, s->batch - b0);
-        lssm_status e = linear(s, m->lm_head, x + (size_t)b0 * h.d_model, s->logits + (size_t)b0 * h.vocab_size, r,
-                               h.vocab_size, h.d_model, m->norm_f, 0, st);
-        if (e) return e;
-    }
-    return LSSM_OK;
+    // one call for all rows: the GEMV kernels for <= 8 rows, else the tensor-core GEMM, so
+    // the lm_head weights are read once per step whatever the batch
+    return linear(s, m->lm_head, x, s->logits, s->batch, h.vocab_size, h.d_model, m->norm_f, 0, st);
 }
 
 static lssm_status check_err(lssm_session* s, const char* what) {
