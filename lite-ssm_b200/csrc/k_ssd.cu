@@ -24,66 +24,67 @@ namespace lssm {
 
 
 // Vector path: each warp owns STEP_R consecutive (b, h, p) state rows with N == 128
-// (one float4 per lane per row); all rows' state, B and C loads are issued before
-// any arithmetic so a warp keeps STEP_R * 512 B of state in flight.
-constexpr int STEP_R = 4;
+// (one float4 per lane per row). P % STEP_R == 0, so a warp's rows share one (b, h):
+// the head's dt / decay are computed once per warp and the row -> (b, h, p) split once,
+// in 32-bit arithmetic. All rows' state loads are issued before any arithmetic, so a
+// warp keeps STEP_R * 512 B of state in flight.
+constexpr int STEP_R = 8;
 
 __global__ void __launch_bounds__(256) k_ssd_step_r4(StepArgs a) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t rows = (uint64_t)a.batch * a.H * a.P;
-    const uint64_t row0 = ((uint64_t)blockIdx.x * 8 + warp) * STEP_R;
+    const uint32_t rows = a.batch * a.H * a.P;
+    const uint32_t row0 = (blockIdx.x * 8 + warp) * STEP_R;
     if (row0 >= rows) return;
+    const uint32_t p0 = row0 % a.P, bh = row0 / a.P, h = bh % a.H, b = bh / a.H;
+    const uint32_t g = h / max(1u, a.H / a.G);
     float4 s[STEP_R];
-    uint2 bu[STEP_R], cu[STEP_R];
-    float decay[STEP_R], dtx[STEP_R], xv[STEP_R];
+#pragma unroll
+    for (int r = 0; r < STEP_R; ++r)
+        s[r] = *reinterpret_cast<const float4*>(a.state + (uint64_t)(row0 + r) * 128 + lane * 4);
+    const uint2 bu = *reinterpret_cast<const uint2*>(a.B + b * a.bc_bs + (uint64_t)g * 128 + lane * 4);
+    const uint2 cu = *reinterpret_cast<const uint2*>(a.C + b * a.bc_bs + (uint64_t)g * 128 + lane * 4);
+    const __half* xrow = a.x + b * a.x_bs + (uint64_t)h * a.P + p0;
+    float xv[STEP_R];
+#pragma unroll
+    for (int r = 0; r < STEP_R; ++r) xv[r] = __half2float(xrow[r]);
+    const float A = -expf(__half2float(a.A_log[h]));
+    const float dt = fminf(fmaxf(softplus(__half2float(a.dt_raw[b * a.dt_bs + h]) + __half2float(a.dt_bias[h])),
+                                 a.dt_min), a.dt_max);
+    const float decay = expf(A * dt);
+    const float Dh = a.has_D ? __half2float(a.D[h]) : 0.0f;
+    const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bu.x));
+    const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bu.y));
+    const float2 c01 = __half22float2(*reinterpret_cast<const __half2*>(&cu.x));
+    const float2 c23 = __half22float2(*reinterpret_cast<const __half2*>(&cu.y));
+    float acc[STEP_R];
 #pragma unroll
     for (int r = 0; r < STEP_R; ++r) {
-        const uint64_t row = min(row0 + r, rows - 1);
-        const uint32_t p = (uint32_t)(row % a.P);
-        const uint32_t h = (uint32_t)((row / a.P) % a.H);
-        const uint32_t b = (uint32_t)(row / ((uint64_t)a.P * a.H));
-        const uint32_t g = h / max(1u, a.H / a.G);
-        s[r] = *reinterpret_cast<const float4*>(a.state + row * 128 + lane * 4);
-        bu[r] = *reinterpret_cast<const uint2*>(a.B + b * a.bc_bs + (uint64_t)g * 128 + lane * 4);
-        cu[r] = *reinterpret_cast<const uint2*>(a.C + b * a.bc_bs + (uint64_t)g * 128 + lane * 4);
-        const float A = -expf(__half2float(a.A_log[h]));
-        const float dt = fminf(fmaxf(softplus(__half2float(a.dt_raw[b * a.dt_bs + h]) + __half2float(a.dt_bias[h])),
-                                     a.dt_min), a.dt_max);
-        decay[r] = expf(A * dt);
-        xv[r] = __half2float(a.x[b * a.x_bs + (uint64_t)h * a.P + p]);
-        dtx[r] = dt * xv[r];
+        const float dtx = dt * xv[r];
+        float4 v = s[r];
+        v.x = decay * v.x + b01.x * dtx;
+        v.y = decay * v.y + b01.y * dtx;
+        v.z = decay * v.z + b23.x * dtx;
+        v.w = decay * v.w + b23.y * dtx;
+        s[r] = v;
+        acc[r] = c01.x * v.x + c01.y * v.y + c23.x * v.z + c23.y * v.w;
     }
 #pragma unroll
-    for (int r = 0; r < STEP_R; ++r) {
-        const uint64_t row = row0 + r;
-        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bu[r].x));
-        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&bu[r].y));
-        const float2 c01 = __half22float2(*reinterpret_cast<const __half2*>(&cu[r].x));
-        const float2 c23 = __half22float2(*reinterpret_cast<const __half2*>(&cu[r].y));
-        float4 v = s[r];
-        v.x = decay[r] * v.x + b01.x * dtx[r];
-        v.y = decay[r] * v.y + b01.y * dtx[r];
-        v.z = decay[r] * v.z + b23.x * dtx[r];
-        v.w = decay[r] * v.w + b23.y * dtx[r];
-        float acc = c01.x * v.x + c01.y * v.y + c23.x * v.z + c23.y * v.w;
-        acc = warp_sum(acc);
-        if (row < rows) {
-            *reinterpret_cast<float4*>(a.state + row * 128 + lane * 4) = v;
-            if (lane == 0) {
-                const uint32_t p = (uint32_t)(row % a.P);
-                const uint32_t h = (uint32_t)((row / a.P) % a.H);
-                const uint32_t b = (uint32_t)(row / ((uint64_t)a.P * a.H));
-                const float Dh = a.has_D ? __half2float(a.D[h]) : 0.0f;
-                const __half yh = __float2half_rn(acc + Dh * xv[r]);
-                const uint64_t o = (uint64_t)h * a.P + p;
-                if (a.z) {
-                    const float zv = __half2float(a.z[b * a.z_bs + o]);
-                    a.y[b * a.y_bs + o] = __float2half_rn(silu(zv) * __half2float(yh));
-                } else {
-                    a.y[b * a.y_bs + o] = yh;
-                }
-            }
-        }
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < STEP_R; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+#pragma unroll
+    for (int r = 0; r < STEP_R; ++r)
+        *reinterpret_cast<float4*>(a.state + (uint64_t)(row0 + r) * 128 + lane * 4) = s[r];
+    // lane r writes row r's output (y, or the gated value half(silu(z) * half(y)))
+    float mine = acc[0], xm = xv[0];
+#pragma unroll
+    for (int r = 1; r < STEP_R; ++r)
+        if ((int)lane == r) { mine = acc[r]; xm = xv[r]; }
+    if (lane < STEP_R) {
+        const uint64_t o = (uint64_t)h * a.P + p0 + lane;
+        const __half yh = __float2half_rn(mine + Dh * xm);
+        if (a.z) a.y[b * a.y_bs + o] = __float2half_rn(silu(__half2float(a.z[b * a.z_bs + o])) * __half2float(yh));
+        else a.y[b * a.y_bs + o] = yh;
     }
 }
 
@@ -150,7 +151,7 @@ cudaError_t launch_ssd_step_ex(const StepArgs& a, cudaStream_t s) {
     if (!rows) return cudaSuccess;
     const bool vec = (a.N % 4 == 0) && aligned(a.state, 16) && aligned(a.B, 8) && aligned(a.C, 8) &&
                      (a.bc_bs % 4 == 0) && (a.G == 1 || a.N % 4 == 0);
-    if (vec && a.N == 128) {
+    if (vec && a.N == 128 && a.P % STEP_R == 0 && rows < (1ull << 31)) {
         k_ssd_step_r4<<<(unsigned)((rows + 8 * STEP_R - 1) / (8 * STEP_R)), 256, 0, s>>>(a);
         return cudaGetLastError();
     }
