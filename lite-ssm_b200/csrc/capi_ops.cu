@@ -344,6 +344,15 @@ lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, co
     CHECK_CTX(ctx);
     if (d.K % 32 != 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "linear_int4_gemm: K must be a multiple of 32");
     if (d.M == 0 || d.N == 0) return finish_op(ctx, "linear_int4_gemm");
+    {
+        const cudaError_t e = launch_gemm_i4(bp(x, x_off), bp(w, w_packed_off), bp(w_scl, w_scales_off), bp(y, y_off),
+                                             d.M, d.N, d.K, 0, ctx->stream);
+        if (e != cudaErrorNotSupported) {
+            if (e != cudaSuccess) return cuda_fail(e, "linear_int4_gemm");
+            return finish_op(ctx, "linear_int4_gemm");
+        }
+        cudaGetLastError();   // clear the not-supported status: dequantise, then the fp16 GEMM
+    }
     void* scratch = nullptr;
     if (lssm_status st = scratch_reserve(ctx, (size_t)d.N * d.K * 2, &scratch)) return st;
     cudaError_t e = launch_int4_dequant_f16(bp(w, w_packed_off), bp(w_scl, w_scales_off), scratch, d.N, d.K,

@@ -751,7 +751,21 @@ static lssm_status linear(lssm_session* s, const TensorRec* w, const __half* x, 
     }
     const void* wf = wp;
     if (w->dtype == DT_INT4_B32) {
-        CU(launch_int4_dequant_f16(wp, static_cast<const uint8_t*>(wp) + (size_t)N * K / 2, s->wscratch, N, K, st));
+        // fused dequant GEMM when the operands allow it; else dequantise to scratch + GEMM
+        const void* sc = static_cast<const uint8_t*>(wp) + (size_t)N * K / 2;
+        __half* out = epilogue == 2 ? s->bout : y;
+        const cudaError_t e = launch_gemm_i4(xin, wp, sc, out, rows, N, K, epilogue == 2 ? 0 : epilogue, st);
+        if (e == cudaSuccess) {
+            s->nl += 1;
+            if (epilogue == 2) {
+                CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
+                s->nl += 1;
+            }
+            return LSSM_OK;
+        }
+        if (e != cudaErrorNotSupported) return cuda_fail(e, "linear: fused INT4 GEMM");
+        cudaGetLastError();
+        CU(launch_int4_dequant_f16(wp, sc, s->wscratch, N, K, st));
         s->nl += 1;
         wf = s->wscratch;
     }

@@ -75,6 +75,10 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
 // `scratch` (N*K halves, caller-owned) and multiplied with the fp16 GEMM.
 cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void* out, uint32_t N, uint32_t K,
                                     cudaStream_t s);
+// INT4 GEMM with the dequantisation fused into the tcgen05 pipeline (k_gemm_i4.cu), same
+// fp16 rounding of each weight; cudaErrorNotSupported when K % 256 or alignment rule it out.
+cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
+                           uint32_t K, int epilogue, cudaStream_t s);
 
 cudaError_t launch_ssd_step(const void* x, const void* B, const void* C, const void* dt_raw, const void* dt_bias,
                             const void* A_log, const void* D, float* state, void* y, uint32_t batch, uint32_t H,
