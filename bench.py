@@ -2,7 +2,7 @@
 decode / prefill tokens per second, with roofline fractions).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload decode27b|ssd|batched]
+                  [--workload decode27b|batched|tp8b]
 
 Default workload (N=1): the Mamba-2 2.7B shape (64 layers, d_model 2560, d_inner 5120,
 80 heads x 64, d_state 128, ngroups 1, vocab 50288), in_proj/out_proj packed INT4_B32 as
@@ -39,6 +39,8 @@ sys.path.insert(0, str(ROOT / "lite-ssm_b200"))
 METRIC = "decode tok/s & prefill tok/s (2.7B quant) at 1/2/4/8 B200; % HBM/tensor roofline"
 HP27 = dict(d_model=2560, n_layer=64, d_state=128, d_conv=4, expand=2, vocab_size=50288, n_heads=80, d_head=64,
             chunk_size=256, n_groups=1, norm_before_gate=0)
+HP8B = dict(d_model=4096, n_layer=56, d_state=128, d_conv=4, expand=2, vocab_size=256000, n_heads=128, d_head=64,
+            chunk_size=256, n_groups=8, norm_before_gate=0)
 PROMPT, NEW = 2048, 512
 VOCAB_IDS = 50280
 
@@ -610,10 +612,106 @@ def run_batched(args, world, rank, local, dist):
     return 0
 
 
+def run_tp8b(args, world, rank, local, dist):
+    """The 8B-shape config: 4 sequences, prefill 4096 random ids + 128 greedy decode tokens,
+    the heads (and groups, d_inner channels, lm_head vocab rows) tensor-parallel over the
+    ranks with NCCL all-reduces after out_proj (and of the gated-norm sum of squares);
+    one GPU runs the unsharded session. Strong scaling (the job is fixed)."""
+    import lssm
+    import torch
+    hbm, _, _, peak_kind = measured_peaks()
+    B, plen, steps_new = args.tp_batch, args.tp_prompt, args.tp_new
+    ctx = lssm.Ctx(local)
+    model = lssm.Model.synthesize(ctx, lssm.hparams(**HP8B), seed=0, int4=True)
+    comm = None
+    if world > 1:
+        uid = torch.zeros(lssm.COMM_ID_BYTES, dtype=torch.uint8, device=f"cuda:{local}")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(lssm.Comm.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = lssm.Comm(ctx, rank, world, bytes(uid.cpu().numpy()))
+    sess = lssm.Session(ctx, model, batch=B, max_seq_len=plen, comm=comm)
+    rng = np.random.default_rng(8000)
+    prompts = rng.integers(0, 255990, size=(B, plen)).astype(np.uint32)   # same on every rank
+
+    def step():
+        sess.reset()
+        first = sess.prefill(prompts)
+        p_ms, _ = sess.timing()
+        toks = sess.decode(first, steps_new)
+        _, d_ms = sess.timing()
+        return p_ms, d_ms, toks
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    for _ in range(args.warmup):
+        step()
+    barrier(dist, local)
+    torch.cuda.synchronize()
+    clocks.mark_begin()
+    pre, dec = [], []
+    w0 = time.time()
+    for _ in range(args.steps):
+        p_ms, d_ms, toks = step()
+        pre.append(p_ms)
+        dec.append(d_ms)
+    torch.cuda.synchronize()
+    wall = time.time() - w0
+    barrier(dist, local)
+    clk = clocks.stop()
+    tot_pre, tot_dec = allreduce_max(dist, [sum(pre), sum(dec)], local)
+    decode_tok_s = B * steps_new * args.steps / (tot_dec / 1000.0)
+    prefill_tok_s = B * plen * args.steps / (tot_pre / 1000.0)
+    pinned = torch.from_numpy(prompts).pin_memory().numpy()
+    barrier(dist, local)
+    t0 = time.perf_counter()
+    out = sess.generate(pinned, steps_new + 1)
+    e_s = time.perf_counter() - t0
+    (e_max,) = allreduce_max(dist, [e_s], local)
+    assert out.shape == (B, steps_new + 1)
+    bpt = decode_bytes_per_token(HP8B)
+    state_b = HP8B["n_layer"] * (bpt["per_layer"]["ssd_state_rw"] + bpt["per_layer"]["conv_state_rw"])
+    step_bytes = (bpt["total"] - state_b + B * state_b) / world   # weights once per step + B states, per GPU
+    ms_step = tot_dec / args.steps / steps_new
+    n_pre, n_dec = sess.launches()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": (tot_pre + tot_dec) / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 activations, int4_b32 weights, f32 accum",
+            "data": "synthetic (seeded random-init weights in the reference .ssm INT4_B32 layout, random prompt ids)",
+            "config": {"workload": f"8B-shape: batch {B}, prefill {plen} + {steps_new} greedy decode tokens",
+                       "model": "mamba2-8b-shape (56L, d_model 4096, 128x64 heads, 8 groups, d_state 128, vocab 256000)",
+                       "global_batch": B, "seq_len": plen,
+                       "parallelism": f"heads tensor-parallel x{world} (NCCL all-reduce after out_proj)" if world > 1
+                       else "one GPU, unsharded",
+                       "l2": f"no flush: each decode step streams {step_bytes / 1e9:.2f} GB per GPU (> 126 MB L2)"},
+            "prefill_tok_s": prefill_tok_s,
+            "decode_ms_per_step": ms_step,
+            "roofline": {"bound": "hbm", "achieved": step_bytes / (ms_step / 1000.0) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm, "traffic": None,
+                         "kernel": "decode step (per-op CUDA graph incl. NCCL)", "bytes_per_step_per_gpu": step_bytes,
+                         "peak_kind": f"{peak_kind} hbm_gbs"},
+            "e2e": {"value": B * (steps_new + 1) / e_max, "unit": "tok/s", "h2d_bytes_per_step": B * plen * 4,
+                    "d2h_bytes_per_step": B * (steps_new + 1) * 4},
+            "gpu_launches": args.steps * (n_pre + n_dec), "clocks": clk, "wall_s": wall,
+        }
+        print(json.dumps(line), flush=True)
+    sess.close()
+    if comm is not None:
+        comm.close()
+    model.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="decode27b", choices=["decode27b", "batched"],
-                    help="decode27b: the headline batch-1 request per GPU; batched: --seqs sequences sharded over GPUs")
+    ap.add_argument("--workload", default="decode27b", choices=["decode27b", "batched", "tp8b"],
+                    help="decode27b: the headline batch-1 request per GPU; batched: --seqs sequences sharded over "
+                         "GPUs; tp8b: the 8B shape, heads tensor-parallel over GPUs")
+    ap.add_argument("--tp-batch", type=int, default=4)
+    ap.add_argument("--tp-prompt", type=int, default=4096)
+    ap.add_argument("--tp-new", type=int, default=128)
     ap.add_argument("--seqs", type=int, default=64)
     ap.add_argument("--batched-prompt", type=int, default=512)
     ap.add_argument("--batched-new", type=int, default=256)
@@ -651,6 +749,8 @@ def main():
     try:
         if args.workload == "batched":
             return run_batched(args, world, rank, local, dist)
+        if args.workload == "tp8b":
+            return run_tp8b(args, world, rank, local, dist)
         return run_ours(args, world, rank, local, dist)
     finally:
         if dist is not None:

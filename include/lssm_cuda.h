@@ -259,6 +259,31 @@ lssm_status lssm_session_launches(lssm_session* s, uint64_t* prefill, uint64_t* 
  *   "trace"      1 = record per-phase %globaltimer stamps of the persistent kernel's first
  *                step (read with lssm_session_trace). */
 lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t value);
+/* ---- multi-GPU: head tensor parallelism (no reference counterpart: the reference is
+ * single-device) ----------------------------------------------------------------------
+ * One rank per GPU. Every rank loads (or synthesises) the same model; a TP session
+ * copies this rank's shard: in_proj rows of its heads / groups ([z | x | B | C | dt]),
+ * its conv channels and head parameters, the matching mixer-norm slice, the out_proj
+ * columns of its d_inner slice (K split) and a vocab slice of lm_head. Per layer two
+ * sum-all-reduces run on the context stream: the per-token sum of squares of the gated
+ * activations (the gated RMSNorm spans the full d_inner, mamba2_block.cpp:235-238) and
+ * the fp32 out_proj partials, rounded to fp16 once before the residual add. lm_head
+ * argmax merges the ranks' (value, index) pairs with the first-max rule. Requires
+ * n_heads and n_groups divisible by the world size. */
+#define LSSM_COMM_ID_BYTES 128
+typedef struct lssm_comm lssm_comm;
+/* NCCL unique id (LSSM_COMM_ID_BYTES bytes) made on one rank; the caller shares it. */
+lssm_status lssm_comm_unique_id(uint8_t* out);
+lssm_status lssm_comm_init(lssm_ctx* ctx, int rank, int world, const uint8_t* id, lssm_comm** out);
+lssm_status lssm_comm_destroy(lssm_comm* c);
+int lssm_comm_rank(const lssm_comm* c);
+int lssm_comm_world(const lssm_comm* c);
+/* A session over this rank's shard of `m` (see above). lssm_prefill / lssm_decode /
+ * lssm_generate / lssm_session_logits are then collective: every rank calls them with the
+ * same tokens. */
+lssm_status lssm_session_create_tp(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch,
+                                   uint32_t max_seq_len, lssm_session** out);
+
 /* Phase trace of the last persistent decode: sm_count x (n_layer * 10 + 6) u64 words.
  * Per layer: [0] layer start, [1] in_proj RMSNorm staged, [2] in_proj + conv done,
  * [3] after grid barrier, [4] ssd_step done, [5] after grid barrier, [6] out_proj RMSNorm

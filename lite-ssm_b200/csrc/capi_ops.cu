@@ -133,6 +133,11 @@ lssm_status lssm_ctx_create(int device, lssm_ctx** out) {
     // The device error word of the bounded waits is allocated here, never lazily
     // inside a later op (which might be running under stream capture).
     if (!tc_error_word()) { lssm_ctx_destroy(c); return fail(LSSM_ERR_OUT_OF_MEMORY, "lssm_ctx_create: error word"); }
+    // Likewise the driver entry point of the tensor-map encoder: looked up here, outside
+    // any capture, so the first tensor-map kernel may be captured into a graph.
+    (void)tensor_map_encoder();
+    gemv_init();
+    cudaGetLastError();
     *out = c;
     return LSSM_OK;
 }

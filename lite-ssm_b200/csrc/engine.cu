@@ -40,9 +40,6 @@ cudaError_t launch_seed_strided(const void* xbc, uint64_t in_stride, void* state
                                 uint32_t K, cudaStream_t s);
 cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
                         cudaStream_t s);
-cudaError_t launch_argmax_pick(const void* logits, uint32_t B, uint32_t V, uint32_t* cur, uint32_t* history,
-                               uint32_t hist_stride, uint32_t* step, const void* embed, void* hidden, uint32_t d_model,
-                               cudaStream_t s);
 cudaError_t launch_synth_f16(void* out, uint64_t n, uint64_t seed, uint64_t stream, float amp, cudaStream_t s);
 cudaError_t launch_synth_int4(void* out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream, float amp,
                               cudaStream_t s);
@@ -473,6 +470,13 @@ extern "C" int lssm_parse_header(const void* bytes, size_t n, lssm_hparams* hp, 
 // ---------------------------------------------------------------------------
 //  Session
 // ---------------------------------------------------------------------------
+// Weights one layer reads: into the model image (one GPU) or this rank's shard (TP).
+struct LayerRef {
+    const uint8_t* in_w; uint32_t in_dt;
+    const uint8_t* out_w; uint32_t out_dt;
+    const __half *conv_w, *conv_b, *dt_bias, *A_log, *D, *norm, *mixer_norm;
+};
+
 struct lssm_session {
     lssm_ctx* ctx = nullptr;
     lssm_model* m = nullptr;
@@ -508,6 +512,20 @@ struct lssm_session {
     const char* persist_why = "";  // why the persistent kernel is not used ("" = it is)
     uint64_t* d_trace = nullptr;   // phase stamps of the persistent kernel's first step
     bool trace_on = false;
+    // Weights and local dims: the model's for one GPU, this rank's shard for TP.
+    std::vector<LayerRef> lw;
+    const uint8_t* lm_w = nullptr; uint32_t lm_dt = 0;
+    const __half* embed = nullptr; const __half* norm_f = nullptr;
+    uint32_t di = 0, xd = 0, proj_dim = 0, GN = 0, H = 0, G = 0, V = 0, v_off = 0, v_max = 0;
+    // head tensor parallelism
+    lssm_comm* comm = nullptr;
+    int tp_rank = 0, tp_world = 1;
+    uint8_t* d_shard = nullptr;
+    float *d_sumsq = nullptr, *d_part32 = nullptr;
+    __half* d_gather = nullptr;    // all ranks' logits, for lssm_session_logits
+    // greedy pick: per-chunk (value, index) pairs, per-row tickets, per-rank row pairs
+    uint2 *d_cpair = nullptr, *d_pair = nullptr;
+    uint32_t* d_ticket = nullptr;
 };
 
 static lssm_status s_alloc(void** p, size_t n, const char* what) {
@@ -523,7 +541,8 @@ extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
     if (s->graph) cudaGraphExecDestroy(s->graph);
     void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
                   s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
-                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart};
+                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart,
+                  s->d_shard, s->d_sumsq, s->d_part32, s->d_gather, s->d_cpair, s->d_pair, s->d_ticket};
     for (void* p : ps)
         if (p) cudaFree(p);
     for (auto& e : s->ev)
@@ -626,8 +645,151 @@ static PParams persist_params(lssm_session* s, uint32_t n_steps) {
     return p;
 }
 
-extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_t batch, uint32_t max_L,
-                                           lssm_session** out) {
+// One GPU: every layer reads the model image.
+static void bind_model_refs(lssm_session* s) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    auto hp = [&](const TensorRec* t) { return reinterpret_cast<const __half*>(m->d_base + t->offset); };
+    s->lw.resize(h.n_layer);
+    for (uint32_t l = 0; l < h.n_layer; ++l) {
+        const LayerW& L = m->layers[l];
+        s->lw[l] = {m->d_base + L.in_proj->offset, L.in_proj->dtype, m->d_base + L.out_proj->offset, L.out_proj->dtype,
+                    hp(L.conv_w), hp(L.conv_b), hp(L.dt_bias), hp(L.A_log), hp(L.D), hp(L.norm), hp(L.mixer_norm)};
+    }
+    s->lm_w = m->d_base + m->lm_head->offset;
+    s->lm_dt = m->lm_head->dtype;
+    s->embed = hp(m->embed);
+    s->norm_f = hp(m->norm_f);
+    s->di = m->d_inner; s->xd = m->xbc; s->proj_dim = m->proj; s->GN = m->GN;
+    s->H = h.n_heads; s->G = h.n_groups; s->V = h.vocab_size; s->v_off = 0; s->v_max = h.vocab_size;
+}
+
+static size_t lin_bytes(uint32_t dt, size_t N, size_t K) { return dt == DT_INT4_B32 ? N * K / 2 + N * K / 32 * 2 : N * K * 2; }
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Head tensor parallelism: copy this rank's shard of every layer out of the model image
+// (rows of its heads / groups for in_proj and conv, its d_inner columns of out_proj,
+// its vocab rows of lm_head) into one device buffer; norms and embeddings stay shared.
+static lssm_status build_tp_shard(lssm_session* s) {
+    lssm_model* m = s->m;
+    const SsmHeader& h = m->img.hdr;
+    const uint32_t T = (uint32_t)s->tp_world, r = (uint32_t)s->tp_rank;
+    const uint32_t dm = h.d_model, di = m->d_inner, GN = m->GN, xd = m->xbc, P = h.d_head, N = h.d_state;
+    const uint32_t dc = h.d_conv;
+    if (h.n_heads % T || h.n_groups % T)
+        return fail(LSSM_ERR_INVALID_ARGUMENT, "tensor parallel: n_heads (%u) and n_groups (%u) must divide by %u ranks",
+                    h.n_heads, h.n_groups, T);
+    const uint32_t Hr = h.n_heads / T, Gr = h.n_groups / T, dir = Hr * P, GNr = Gr * N, xdr = dir + 2 * GNr;
+    const uint32_t projr = dir + xdr + Hr;
+    if (dir % 32) return fail(LSSM_ERR_INVALID_ARGUMENT, "tensor parallel: d_inner slice %u is not a multiple of 32", dir);
+    const uint32_t vmax = (h.vocab_size + T - 1) / T, voff = std::min(h.vocab_size, r * vmax);
+    const uint32_t Vr = std::min(vmax, h.vocab_size - voff);
+    // sizes
+    size_t total = 0;
+    std::vector<size_t> off_in(h.n_layer), off_out(h.n_layer), off_cw(h.n_layer), off_cb(h.n_layer), off_dtb(h.n_layer),
+        off_al(h.n_layer), off_D(h.n_layer), off_mn(h.n_layer);
+    for (uint32_t l = 0; l < h.n_layer; ++l) {
+        const LayerW& L = m->layers[l];
+        off_in[l] = total; total += al256(lin_bytes(L.in_proj->dtype, projr, dm));
+        off_out[l] = total; total += al256(lin_bytes(L.out_proj->dtype, dm, dir));
+        off_cw[l] = total; total += al256((size_t)xdr * dc * 2);
+        off_cb[l] = total; total += al256((size_t)xdr * 2);
+        off_dtb[l] = total; total += al256((size_t)Hr * 2);
+        off_al[l] = total; total += al256((size_t)Hr * 2);
+        off_D[l] = total; total += al256((size_t)Hr * 2);
+        off_mn[l] = total; total += al256((size_t)dir * 2);
+    }
+    const size_t off_lm = total;
+    total += al256(lin_bytes(m->lm_head->dtype, Vr, dm));
+    if (lssm_status st = s_alloc(reinterpret_cast<void**>(&s->d_shard), total, "tensor parallel: shard")) return st;
+    cudaStream_t st = s->ctx->stream;
+    uint8_t* base = s->d_shard;
+    const uint8_t* img = m->d_base;
+    auto cp = [&](void* dst, const void* src, size_t n) -> cudaError_t {
+        return n ? cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, st) : cudaSuccess;
+    };
+    // row segments (model row, rows) of this rank's in_proj rows: [z | x | B | C | dt]
+    const uint32_t seg_src[5] = {r * dir, di + r * dir, 2 * di + r * GNr, 2 * di + GN + r * GNr, di + xd + r * Hr};
+    const uint32_t seg_n[5] = {dir, dir, GNr, GNr, Hr};
+    // channel segments of the conv weights / bias: [x | B | C]
+    const uint32_t ch_src[3] = {r * dir, di + r * GNr, di + GN + r * GNr};
+    const uint32_t ch_n[3] = {dir, GNr, GNr};
+    s->lw.resize(h.n_layer);
+    cudaError_t e = cudaSuccess;
+    auto hp = [&](const TensorRec* t) { return reinterpret_cast<const __half*>(img + t->offset); };
+    for (uint32_t l = 0; l < h.n_layer && e == cudaSuccess; ++l) {
+        const LayerW& L = m->layers[l];
+        // in_proj rows
+        const uint8_t* src = img + L.in_proj->offset;
+        uint8_t* dst = base + off_in[l];
+        if (L.in_proj->dtype == DT_INT4_B32) {
+            const size_t rb = dm / 2, sb = dm / 32 * 2;
+            const uint8_t* ssc = src + (size_t)m->proj * rb;
+            uint8_t* dsc = dst + (size_t)projr * rb;
+            for (uint32_t sg = 0, row = 0; sg < 5; row += seg_n[sg], ++sg) {
+                if (e == cudaSuccess) e = cp(dst + (size_t)row * rb, src + (size_t)seg_src[sg] * rb, (size_t)seg_n[sg] * rb);
+                if (e == cudaSuccess) e = cp(dsc + (size_t)row * sb, ssc + (size_t)seg_src[sg] * sb, (size_t)seg_n[sg] * sb);
+            }
+        } else {
+            const size_t rb = (size_t)dm * 2;
+            for (uint32_t sg = 0, row = 0; sg < 5; row += seg_n[sg], ++sg)
+                if (e == cudaSuccess) e = cp(dst + (size_t)row * rb, src + (size_t)seg_src[sg] * rb, (size_t)seg_n[sg] * rb);
+        }
+        // out_proj columns [r * dir, (r + 1) * dir) of every row (K split)
+        const uint8_t* osrc = img + L.out_proj->offset;
+        uint8_t* odst = base + off_out[l];
+        if (L.out_proj->dtype == DT_INT4_B32) {
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(odst, dir / 2, osrc + (size_t)r * dir / 2, di / 2, dir / 2, dm,
+                                      cudaMemcpyDeviceToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(odst + (size_t)dm * dir / 2, dir / 32 * 2, osrc + (size_t)dm * di / 2 + (size_t)r * dir / 32 * 2,
+                                      di / 32 * 2, dir / 32 * 2, dm, cudaMemcpyDeviceToDevice, st);
+        } else if (e == cudaSuccess) {
+            e = cudaMemcpy2DAsync(odst, (size_t)dir * 2, osrc + (size_t)r * dir * 2, (size_t)di * 2, (size_t)dir * 2, dm,
+                                  cudaMemcpyDeviceToDevice, st);
+        }
+        // conv weights / bias channels, head parameters, mixer-norm slice
+        for (uint32_t sg = 0, ch = 0; sg < 3; ch += ch_n[sg], ++sg) {
+            if (e == cudaSuccess)
+                e = cp(base + off_cw[l] + (size_t)ch * dc * 2, img + L.conv_w->offset + (size_t)ch_src[sg] * dc * 2,
+                       (size_t)ch_n[sg] * dc * 2);
+            if (e == cudaSuccess)
+                e = cp(base + off_cb[l] + (size_t)ch * 2, img + L.conv_b->offset + (size_t)ch_src[sg] * 2, (size_t)ch_n[sg] * 2);
+        }
+        if (e == cudaSuccess) e = cp(base + off_dtb[l], img + L.dt_bias->offset + (size_t)r * Hr * 2, (size_t)Hr * 2);
+        if (e == cudaSuccess) e = cp(base + off_al[l], img + L.A_log->offset + (size_t)r * Hr * 2, (size_t)Hr * 2);
+        if (e == cudaSuccess) e = cp(base + off_D[l], img + L.D->offset + (size_t)r * Hr * 2, (size_t)Hr * 2);
+        if (e == cudaSuccess) e = cp(base + off_mn[l], img + L.mixer_norm->offset + (size_t)r * dir * 2, (size_t)dir * 2);
+        auto bh = [&](size_t o) { return reinterpret_cast<const __half*>(base + o); };
+        s->lw[l] = {base + off_in[l], L.in_proj->dtype, base + off_out[l], L.out_proj->dtype, bh(off_cw[l]),
+                    bh(off_cb[l]), bh(off_dtb[l]), bh(off_al[l]), bh(off_D[l]), hp(L.norm), bh(off_mn[l])};
+    }
+    // lm_head vocab rows [voff, voff + Vr)
+    if (e == cudaSuccess) {
+        const uint8_t* lsrc = img + m->lm_head->offset;
+        if (m->lm_head->dtype == DT_INT4_B32) {
+            const size_t rb = dm / 2, sb = dm / 32 * 2;
+            e = cp(base + off_lm, lsrc + (size_t)voff * rb, (size_t)Vr * rb);
+            if (e == cudaSuccess)
+                e = cp(base + off_lm + (size_t)Vr * rb, lsrc + (size_t)h.vocab_size * rb + (size_t)voff * sb, (size_t)Vr * sb);
+        } else {
+            e = cp(base + off_lm, lsrc + (size_t)voff * dm * 2, (size_t)Vr * dm * 2);
+        }
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor parallel: shard copies");
+    s->lm_w = base + off_lm;
+    s->lm_dt = m->lm_head->dtype;
+    s->embed = hp(m->embed);
+    s->norm_f = hp(m->norm_f);
+    s->di = dir; s->xd = xdr; s->proj_dim = projr; s->GN = GNr; s->H = Hr; s->G = Gr;
+    s->V = Vr; s->v_off = voff; s->v_max = vmax;
+    return LSSM_OK;
+}
+
+static lssm_status session_create_impl(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch, uint32_t max_L,
+                                       lssm_session** out) {
     if (!ctx || !m || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: null argument");
     if (batch == 0 || max_L == 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: batch and max_seq_len must be >= 1");
     cudaSetDevice(ctx->device);
@@ -638,38 +800,54 @@ extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_
     s->batch = batch;
     s->max_L = max_L;
     const SsmHeader& h = m->img.hdr;
-    const size_t rows = (size_t)batch * max_L;
-    s->conv_layer = (size_t)batch * m->xbc * h.d_conv;
-    s->ssd_layer = (size_t)batch * h.n_heads * h.d_head * h.d_state;
     lssm_status st;
+    s->comm = comm;
+    s->tp_rank = comm_rank(comm);
+    s->tp_world = comm_world(comm);
+    if (comm) {
+        if ((st = build_tp_shard(s.get()))) return st;
+    } else {
+        bind_model_refs(s.get());
+    }
+    const size_t rows = (size_t)batch * max_L;
+    s->conv_layer = (size_t)batch * s->xd * h.d_conv;
+    s->ssd_layer = (size_t)batch * s->H * h.d_head * h.d_state;
 #define SA(ptr, n, what) if ((st = s_alloc(reinterpret_cast<void**>(&ptr), n, what))) return st
     SA(s->conv, s->conv_layer * h.n_layer * 2, "session: conv state");
     SA(s->ssd, s->ssd_layer * h.n_layer * 4, "session: ssd state");
     SA(s->hidden, rows * h.d_model * 2, "session: hidden");
     // normed holds the RMSNorm output of either linear's input (d_model for in_proj,
     // d_inner for out_proj), so it is sized for the wider of the two.
-    SA(s->normed, rows * std::max<size_t>(h.d_model, m->d_inner) * 2, "session: normed");
-    SA(s->proj, rows * m->proj * 2, "session: proj");
-    SA(s->xs, rows * m->d_inner * 2, "session: x");
-    SA(s->Bs, rows * m->GN * 2, "session: B");
-    SA(s->Cs, rows * m->GN * 2, "session: C");
-    SA(s->ys, rows * m->d_inner * 2, "session: y");
-    SA(s->gated, rows * m->d_inner * 2, "session: gated");
-    SA(s->mixn, rows * m->d_inner * 2, "session: mixer norm");
+    SA(s->normed, rows * std::max<size_t>(h.d_model, s->di) * 2, "session: normed");
+    SA(s->proj, rows * s->proj_dim * 2, "session: proj");
+    SA(s->xs, rows * s->di * 2, "session: x");
+    SA(s->Bs, rows * s->GN * 2, "session: B");
+    SA(s->Cs, rows * s->GN * 2, "session: C");
+    SA(s->ys, rows * s->di * 2, "session: y");
+    SA(s->gated, rows * s->di * 2, "session: gated");
+    SA(s->mixn, rows * s->di * 2, "session: mixer norm");
     SA(s->bout, rows * h.d_model * 2, "session: block out");
-    SA(s->logits, (size_t)batch * h.vocab_size * 2, "session: logits");
+    SA(s->logits, (size_t)batch * s->v_max * 2, "session: logits");
     SA(s->lastrows, (size_t)batch * h.d_model * 2, "session: last rows");
     SA(s->d_tokens, rows * 4, "session: tokens");
     SA(s->d_cur, (size_t)batch * 4, "session: current tokens");
     SA(s->d_step, 16, "session: step");
     SA(s->d_err, 16, "session: error word");
+    if (comm) {
+        SA(s->d_sumsq, rows * 4, "session: TP sum of squares");
+        SA(s->d_part32, rows * h.d_model * 4, "session: TP out_proj partials");
+    }
+    SA(s->d_cpair, (size_t)batch * argmax_chunks(s->V) * sizeof(uint2), "session: argmax chunk pairs");
+    SA(s->d_pair, (size_t)s->tp_world * batch * sizeof(uint2), "session: argmax row pairs");
+    SA(s->d_ticket, (size_t)batch * 4, "session: argmax tickets");
+    cudaMemsetAsync(s->d_ticket, 0, (size_t)batch * 4, ctx->stream);
     bool any_int4 = false;
     size_t wmax = 0;
-    for (auto& L : m->layers) {
-        if (L.in_proj->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)m->proj * h.d_model); }
-        if (L.out_proj->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.d_model * m->d_inner); }
+    for (auto& L : s->lw) {
+        if (L.in_dt == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)s->proj_dim * h.d_model); }
+        if (L.out_dt == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.d_model * s->di); }
     }
-    if (m->lm_head->dtype == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.vocab_size * h.d_model); }
+    if (s->lm_dt == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)s->V * h.d_model); }
     if (any_int4) {
         SA(s->wscratch, wmax * 2, "session: dequant scratch");
         s->wscratch_elems = wmax;
@@ -677,10 +855,22 @@ extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_
 #undef SA
     for (auto& e : s->ev) cudaEventCreate(&e);
     cudaMemsetAsync(s->d_err, 0, 16, ctx->stream);
-    if ((st = setup_persistent(s.get()))) return st;
+    if (!comm && (st = setup_persistent(s.get()))) return st;
+    if (comm) s->persist_why = "tensor-parallel session";
     if ((st = lssm_session_reset(s.get()))) return st;
     *out = s.release();
     return LSSM_OK;
+}
+
+extern "C" lssm_status lssm_session_create(lssm_ctx* ctx, lssm_model* m, uint32_t batch, uint32_t max_L,
+                                           lssm_session** out) {
+    return session_create_impl(ctx, m, nullptr, batch, max_L, out);
+}
+
+extern "C" lssm_status lssm_session_create_tp(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch,
+                                              uint32_t max_L, lssm_session** out) {
+    if (!comm) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create_tp: null communicator");
+    return session_create_impl(ctx, m, comm, batch, max_L, out);
 }
 
 extern "C" lssm_status lssm_session_reset(lssm_session* s) {
@@ -726,35 +916,33 @@ extern "C" lssm_status lssm_session_set_option(lssm_session* s, const char* key,
 
 static inline const void* W(const lssm_model* m, const TensorRec* t) { return m->d_base + t->offset; }
 
-// Linear over `rows` activation rows with a .ssm weight (f16 or INT4_B32): Y = X W^T.
-// rows <= 8 uses the GEMV kernels (optionally with fused RMSNorm / residual),
-// otherwise the tensor-core GEMM (INT4 dequantised to fp16 scratch first).
-static lssm_status linear(lssm_session* s, const TensorRec* w, const __half* x, __half* y, uint32_t rows, uint32_t N,
-                          uint32_t K, const TensorRec* prenorm, int epilogue, cudaStream_t st) {
-    const lssm_model* m = s->m;
-    const void* wp = W(m, w);
+// Linear over `rows` activation rows with weight `wp` (f16 or INT4_B32, .ssm layout): Y = X W^T.
+// rows <= 8 uses the GEMV kernels (optionally with fused RMSNorm / residual), otherwise
+// the tensor-core GEMM (INT4: fused dequant for small M, else dequantised to scratch).
+// epilogue: 0 store fp16, 1 SiLU, 2 residual add into y, 3 store fp32 (y is float*).
+static lssm_status linear(lssm_session* s, const uint8_t* wp, uint32_t dtype, const __half* x, void* y, uint32_t rows,
+                          uint32_t N, uint32_t K, const __half* prenorm, int epilogue, cudaStream_t st) {
     if (rows <= 8) {
-        const void* nw = prenorm ? W(m, prenorm) : nullptr;
-        if (w->dtype == DT_INT4_B32)
-            CU(launch_gemv_int4_ex(x, wp, static_cast<const uint8_t*>(wp) + (size_t)N * K / 2, y, rows, N, K, nw, 1e-5f,
-                                   epilogue, st));
+        if (dtype == DT_INT4_B32)
+            CU(launch_gemv_int4_ex(x, wp, wp + (size_t)N * K / 2, y, rows, N, K, prenorm, 1e-5f, epilogue, st));
         else
-            CU(launch_gemv_f16(x, wp, y, rows, N, K, nw, 1e-5f, epilogue, st));
+            CU(launch_gemv_f16(x, wp, y, rows, N, K, prenorm, 1e-5f, epilogue, st));
         s->nl += 1;
         return LSSM_OK;
     }
     const __half* xin = x;
     if (prenorm) {
-        CU(launch_rmsnorm_f16(x, W(m, prenorm), s->normed, rows, K, 1e-5f, st));
+        CU(launch_rmsnorm_f16(x, prenorm, s->normed, rows, K, 1e-5f, st));
         s->nl += 1;
         xin = s->normed;
     }
+    const int gemm_epi = epilogue == 2 ? 0 : epilogue;
+    void* out = epilogue == 2 ? static_cast<void*>(s->bout) : y;
     const void* wf = wp;
-    if (w->dtype == DT_INT4_B32) {
+    if (dtype == DT_INT4_B32) {
         // fused dequant GEMM when the operands allow it; else dequantise to scratch + GEMM
-        const void* sc = static_cast<const uint8_t*>(wp) + (size_t)N * K / 2;
-        __half* out = epilogue == 2 ? s->bout : y;
-        const cudaError_t e = launch_gemm_i4(xin, wp, sc, out, rows, N, K, epilogue == 2 ? 0 : epilogue, st);
+        const void* sc = wp + (size_t)N * K / 2;
+        const cudaError_t e = launch_gemm_i4(xin, wp, sc, out, rows, N, K, gemm_epi, st);
         if (e == cudaSuccess) {
             s->nl += 1;
             if (epilogue == 2) {
@@ -769,55 +957,51 @@ static lssm_status linear(lssm_session* s, const TensorRec* w, const __half* x, 
         s->nl += 1;
         wf = s->wscratch;
     }
+    CU(launch_gemm_f16(xin, wf, out, rows, N, K, gemm_epi, st));
+    s->nl += 1;
     if (epilogue == 2) {
-        CU(launch_gemm_f16(xin, wf, s->bout, rows, N, K, 0, st));
         CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
-        s->nl += 2;
-    } else {
-        CU(launch_gemm_f16(xin, wf, y, rows, N, K, epilogue, st));
         s->nl += 1;
     }
     return LSSM_OK;
 }
 
-// One Mamba-2 block over rows = batch * L activation rows (decode: L == 1).
+// One Mamba-2 block over rows = batch * L activation rows (decode: L == 1), on this
+// session's weights and local dims (a rank's shard under tensor parallelism).
 static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool decode, cudaStream_t st) {
     lssm_model* m = s->m;
     const SsmHeader& h = m->img.hdr;
-    const LayerW& lw = m->layers[layer];
-    const uint32_t B = s->batch, rows = B * L, dm = h.d_model, di = m->d_inner, GN = m->GN, xd = m->xbc,
-                   proj = m->proj, H = h.n_heads, P = h.d_head, N = h.d_state, Kc = h.d_conv;
+    const LayerRef& lw = s->lw[layer];
+    const uint32_t B = s->batch, rows = B * L, dm = h.d_model, di = s->di, GN = s->GN, xd = s->xd, proj = s->proj_dim,
+                   H = s->H, P = h.d_head, N = h.d_state, Kc = h.d_conv;
     __half* conv = reinterpret_cast<__half*>(s->conv) + s->conv_layer * layer;
     float* ssd = s->ssd + s->ssd_layer * layer;
     lssm_status r;
     // 1+2. RMSNorm + in_proj over [z | xBC | dt]
-    if ((r = linear(s, lw.in_proj, s->hidden, s->proj, rows, proj, dm, lw.norm, 0, st))) return r;
+    if ((r = linear(s, lw.in_w, lw.in_dt, s->hidden, s->proj, rows, proj, dm, lw.norm, 0, st))) return r;
     const __half* zc = s->proj;
     const __half* xbc = s->proj + di;
     const __half* dtc = s->proj + di + xd;
     if (decode) {
         // 3+4. conv update + SiLU + split
-        CU(launch_conv_update_silu_split(xbc, proj, conv, W(m, lw.conv_w), W(m, lw.conv_b), s->xs, s->Bs, s->Cs, B, di,
-                                         GN, Kc, st));
+        CU(launch_conv_update_silu_split(xbc, proj, conv, lw.conv_w, lw.conv_b, s->xs, s->Bs, s->Cs, B, di, GN, Kc, st));
         // 5+6. ssd_step with the fused gate -> gated
         StepArgs a{};
         a.x = s->xs; a.B = s->Bs; a.C = s->Cs; a.dt_raw = dtc;
-        a.dt_bias = static_cast<const __half*>(W(m, lw.dt_bias));
-        a.A_log = static_cast<const __half*>(W(m, lw.A_log));
-        a.D = static_cast<const __half*>(W(m, lw.D));
+        a.dt_bias = lw.dt_bias; a.A_log = lw.A_log; a.D = lw.D;
         a.state = ssd; a.y = s->gated; a.z = zc;
-        a.batch = B; a.H = H; a.P = P; a.N = N; a.G = h.n_groups;
+        a.batch = B; a.H = H; a.P = P; a.N = N; a.G = s->G;
         a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
         a.x_bs = di; a.bc_bs = GN; a.dt_bs = proj; a.y_bs = di; a.z_bs = proj;
         CU(launch_ssd_step_ex(a, st));
         s->nl += 2;
     } else {
-        CU(launch_conv_silu_split(xbc, proj, W(m, lw.conv_w), W(m, lw.conv_b), s->xs, s->Bs, s->Cs, B, L, di, GN, Kc, st));
+        CU(launch_conv_silu_split(xbc, proj, lw.conv_w, lw.conv_b, s->xs, s->Bs, s->Cs, B, L, di, GN, Kc, st));
         SsdArgs a{};
         a.X = s->xs; a.B = s->Bs; a.C = s->Cs; a.dt_raw = dtc;
-        a.dt_bias = W(m, lw.dt_bias); a.A_log = W(m, lw.A_log); a.D = W(m, lw.D);
+        a.dt_bias = lw.dt_bias; a.A_log = lw.A_log; a.D = lw.D;
         a.Y = s->ys; a.state = ssd;
-        a.batch = B; a.L = L; a.H = H; a.P = P; a.N = N; a.G = h.n_groups; a.chunk = h.chunk_size;
+        a.batch = B; a.L = L; a.H = H; a.P = P; a.N = N; a.G = s->G; a.chunk = h.chunk_size;
         a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
         a.x_dtype = 0; a.dt_dtype = 0; a.param_dtype = 0; a.y_dtype = 0;
         a.x_row_stride = di; a.bc_row_stride = GN; a.dt_row_stride = proj; a.y_row_stride = di;
@@ -826,7 +1010,20 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         s->nl += 3;
     }
     // 7+8+9. gated RMSNorm + out_proj + residual add into hidden
-    if ((r = linear(s, lw.out_proj, s->gated, s->hidden, rows, dm, di, lw.mixer_norm, 2, st))) return r;
+    if (s->comm) {
+        // the gated RMSNorm spans the full d_inner: all-reduce each row's sum of squares; the
+        // out_proj partials of this rank's d_inner columns are summed in fp32 across the ranks
+        // and rounded to fp16 once before the residual add
+        CU(launch_rowsumsq(s->gated, di, rows, di, s->d_sumsq, st));
+        if ((r = comm_allreduce_f32(s->comm, s->d_sumsq, rows, st))) return r;
+        CU(launch_rmsnorm_total(s->gated, di, lw.mixer_norm, s->d_sumsq, rows, di, m->d_inner, 1e-5f, s->mixn, st));
+        if ((r = linear(s, lw.out_w, lw.out_dt, s->mixn, s->d_part32, rows, dm, di, nullptr, 3, st))) return r;
+        if ((r = comm_allreduce_f32(s->comm, s->d_part32, (size_t)rows * dm, st))) return r;
+        CU(launch_residual_f32(s->hidden, s->d_part32, (uint64_t)rows * dm, st));
+        s->nl += 3;
+    } else if ((r = linear(s, lw.out_w, lw.out_dt, s->gated, s->hidden, rows, dm, di, lw.mixer_norm, 2, st))) {
+        return r;
+    }
     // 10. seed conv state from pre-conv xBC after a prefill
     if (!decode) {
         CU(launch_seed_strided(xbc, proj, conv, B, L, xd, Kc, st));
@@ -835,13 +1032,28 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
     return LSSM_OK;
 }
 
-// norm_f + lm_head over `x` (batch rows, contiguous) -> logits (batch, vocab) fp16.
-static lssm_status logits_of(lssm_session* s, const __half* x, cudaStream_t st) {
+// norm_f + lm_head over `x` (batch rows, contiguous) -> logits, then the greedy token:
+// d_cur; with `decode`, also history[step] and hidden = embed(next) for the next step.
+// Under tensor parallelism the logits are this rank's vocab slice and the ranks merge
+// their (value, index) first-max pairs.
+static lssm_status pick_tokens(lssm_session* s, const __half* x, bool decode, cudaStream_t st) {
     lssm_model* m = s->m;
     const SsmHeader& h = m->img.hdr;
     // one call for all rows: the GEMV kernels for <= 8 rows, else the tensor-core GEMM, so
     // the lm_head weights are read once per step whatever the batch
-    return linear(s, m->lm_head, x, s->logits, s->batch, h.vocab_size, h.d_model, m->norm_f, 0, st);
+    if (lssm_status r = linear(s, s->lm_w, s->lm_dt, x, s->logits, s->batch, s->V, h.d_model, s->norm_f, 0, st)) return r;
+    uint32_t* hist = decode ? s->d_hist : nullptr;
+    uint32_t* step = decode ? s->d_step : nullptr;
+    const __half* emb = decode ? s->embed : nullptr;
+    __half* hid = decode ? s->hidden : nullptr;
+    const size_t B = s->batch, rk = (size_t)s->tp_rank;
+    CU(launch_argmax_chunks(s->logits, s->V, s->batch, s->V, s->v_off, s->d_cpair, s->d_ticket, s->d_pair + rk * B, st));
+    if (s->comm)
+        if (lssm_status r = comm_allgather(s->comm, s->d_pair + rk * B, s->d_pair, B * sizeof(uint2), st)) return r;
+    CU(launch_argmax_merge(s->d_pair, (uint32_t)s->tp_world, s->batch, s->d_cur, hist, s->hist_cap, step, emb, hid,
+                           h.d_model, st));
+    s->nl += decode ? 3 : 2;
+    return LSSM_OK;
 }
 
 static lssm_status check_err(lssm_session* s, const char* what) {
@@ -881,9 +1093,7 @@ extern "C" lssm_status lssm_prefill(lssm_session* s, const uint32_t* tokens, uin
     // last row of each sequence -> contiguous (batch, d_model)
     CU(cudaMemcpy2DAsync(s->lastrows, (size_t)h.d_model * 2, s->hidden + (size_t)(L - 1) * h.d_model,
                          (size_t)L * h.d_model * 2, (size_t)h.d_model * 2, s->batch, cudaMemcpyDeviceToDevice, st));
-    if (lssm_status r = logits_of(s, s->lastrows, st)) return r;
-    CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, nullptr, 0, nullptr, nullptr, nullptr, 0, st));
-    s->nl += 1;
+    if (lssm_status r = pick_tokens(s, s->lastrows, false, st)) return r;
     s->prefill_launches = s->nl - nl0;
     CU(cudaEventRecord(s->ev[1], st));
     if (next_tokens) CU(cudaMemcpyAsync(next_tokens, s->d_cur, (size_t)s->batch * 4, cudaMemcpyDeviceToHost, st));
@@ -900,11 +1110,7 @@ static lssm_status decode_step_body(lssm_session* s, cudaStream_t st) {
     const SsmHeader& h = m->img.hdr;
     for (uint32_t l = 0; l < h.n_layer; ++l)
         if (lssm_status r = run_block(s, l, 1, true, st)) return r;
-    if (lssm_status r = logits_of(s, s->hidden, st)) return r;
-    CU(launch_argmax_pick(s->logits, s->batch, h.vocab_size, s->d_cur, s->d_hist, s->hist_cap, s->d_step, W(m, m->embed),
-                          s->hidden, h.d_model, st));
-    s->nl += 2;
-    return LSSM_OK;
+    return pick_tokens(s, s->hidden, true, st);
 }
 
 extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint32_t n_steps, uint32_t* out_tokens) {
@@ -1006,13 +1212,30 @@ extern "C" lssm_status lssm_session_logits(lssm_session* s, float* out) {
     if (!s || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_logits: null argument");
     if (!s->logits_valid) return fail(LSSM_ERR_STATE, "lssm_session_logits: no logits computed yet");
     const SsmHeader& h = s->m->img.hdr;
+    auto f = [](uint16_t v) { return __half2float(*reinterpret_cast<__half*>(&v)); };
+    if (s->comm) {
+        // collective: gather every rank's vocab slice (batch x v_max each, rank-major)
+        const size_t per = (size_t)s->batch * s->v_max, W = (size_t)s->tp_world;
+        if (!s->d_gather) {
+            if (lssm_status st = s_alloc(reinterpret_cast<void**>(&s->d_gather), per * W * 2, "session: logits gather"))
+                return st;
+        }
+        if (lssm_status st = comm_allgather(s->comm, s->logits, s->d_gather, per * 2, s->ctx->stream)) return st;
+        std::vector<uint16_t> tmp(per * W);
+        CU(cudaStreamSynchronize(s->ctx->stream));
+        CU(cudaMemcpy(tmp.data(), s->d_gather, per * W * 2, cudaMemcpyDeviceToHost));
+        for (size_t r = 0; r < W; ++r) {
+            const size_t voff = std::min<size_t>(h.vocab_size, r * s->v_max);
+            const size_t vr = std::min<size_t>(s->v_max, h.vocab_size - voff);
+            for (size_t b = 0; b < s->batch; ++b)
+                for (size_t j = 0; j < vr; ++j) out[b * h.vocab_size + voff + j] = f(tmp[r * per + b * vr + j]);
+        }
+        return LSSM_OK;
+    }
     const size_t n = (size_t)s->batch * h.vocab_size;
     std::vector<uint16_t> tmp(n);
     CU(cudaMemcpy(tmp.data(), s->logits, n * 2, cudaMemcpyDeviceToHost));
-    for (size_t i = 0; i < n; ++i) {
-        __half hv = *reinterpret_cast<__half*>(&tmp[i]);
-        out[i] = __half2float(hv);
-    }
+    for (size_t i = 0; i < n; ++i) out[i] = f(tmp[i]);
     return LSSM_OK;
 }
 

@@ -128,28 +128,6 @@ __device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, vola
     }
 }
 
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
-                                     uint32_t bar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ void tma2(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint32_t bar,
-                                     uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
-        : "memory");
-}
-
 // Grid barrier over the consumer threads of every CTA (the producer warp never joins).
 __device__ __forceinline__ bool grid_sync(const PParams& p, uint32_t& gen, volatile int* abort) {
     cons_sync();
@@ -913,25 +891,11 @@ uint32_t odd_seg(uint32_t total) {
     return 1;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    });
-    return fn;
-}
-
 // [rows][segs][128 B] view of a row-major matrix with `row_bytes` per row; box = 16 rows
 // x seg segments, 128-byte swizzle; f16 selects the element type (fp16 rows, or bytes
 // holding INT4 nibble pairs).
 bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t seg, bool f16) {
-    auto enc = encode_tiled();
+    auto enc = tensor_map_encoder();
     if (!enc) return false;
     const uint64_t esz = f16 ? 2 : 1;
     cuuint64_t dims[3] = {128 / esz, row_bytes / 128, rows};
@@ -945,7 +909,7 @@ bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_byte
 
 // INT4_B32 scales [rows][K/32] fp16; box = 16 rows x seg*8 scales, no swizzle.
 bool map_scales(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t seg) {
-    auto enc = encode_tiled();
+    auto enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[2] = {K / 32, rows};
     cuuint64_t strides[1] = {K / 16};

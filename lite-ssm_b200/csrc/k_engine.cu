@@ -4,9 +4,6 @@
 //   * conv1d + SiLU + split     (conv1d.metal:63-137 + activations.metal:49-73, fused;
 //                                reads the xBC columns of the packed in_proj output)
 //   * mixer gate                (activations.metal:76-87 on strided z)
-//   * greedy argmax + next-step embedding gather (sampler.cpp:13-21 first-max rule,
-//     read_logits_fp32 mamba2_model.cpp:177-211 — fp16 -> fp32 is exact, so comparing
-//     fp16 values is comparing the reference's fp32 logits)
 //   * seeded synthetic weights in the .ssm payload layout (INT4_B32 packing restating
 //     tools/export_mamba2.py:68-103 bit for bit).
 #include "device_util.cuh"
@@ -160,75 +157,6 @@ cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* o
     if (g > 148 * 32) g = 148 * 32;
     k_gate<<<(unsigned)g, 256, 0, s>>>(static_cast<const __half*>(z), z_stride, static_cast<const __half*>(y),
                                        static_cast<__half*>(out), rows, d);
-    return cudaGetLastError();
-}
-
-// Greedy pick per sequence (first max, NaN never wins; logits[0] NaN -> id 0 like the
-// reference loop), written to cur[b] and history[b * hist_stride + *step]; optionally
-// gathers the picked token's embedding into hidden[b] for the next decode step.
-// One CTA per sequence; thread 0 of CTA 0 advances *step after all CTAs have read it
-// (the counter is advanced by a separate single-thread kernel to avoid a race).
-__global__ void __launch_bounds__(1024) k_argmax_pick(const __half* __restrict__ logits, uint32_t V,
-                                                      uint32_t* __restrict__ cur, uint32_t* __restrict__ history,
-                                                      uint32_t hist_stride, const uint32_t* __restrict__ step,
-                                                      const __half* __restrict__ embed, __half* __restrict__ hidden,
-                                                      uint32_t d_model) {
-    __shared__ float sv[32];
-    __shared__ uint32_t si[32];
-    __shared__ uint32_t pick;
-    const uint32_t b = blockIdx.x;
-    const __half* lg = logits + (uint64_t)b * V;
-    float bv = -INFINITY;
-    uint32_t bi = 0xFFFFFFFFu;
-    for (uint32_t i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = __half2float(lg[i]);
-        if (v > bv) { bv = v; bi = i; }       // strict: keeps the first index within a thread
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
-    __syncthreads();
-    if (wid == 0) {
-        const uint32_t nw = blockDim.x >> 5;
-        bv = lane < nw ? sv[lane] : -INFINITY;
-        bi = lane < nw ? si[lane] : 0xFFFFFFFFu;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == 0) {
-            const float v0 = __half2float(lg[0]);
-            uint32_t p = (bi == 0xFFFFFFFFu) ? 0u : bi;
-            if (v0 != v0) p = 0;               // NaN at index 0 never gets replaced in the reference loop
-            pick = p;
-            cur[b] = p;
-            if (history) history[(uint64_t)b * hist_stride + (step ? *step : 0)] = p;
-        }
-    }
-    __syncthreads();
-    if (embed) {
-        const __half* src = embed + (uint64_t)pick * d_model;
-        __half* dst = hidden + (uint64_t)b * d_model;
-        for (uint32_t i = threadIdx.x; i < d_model; i += blockDim.x) dst[i] = src[i];
-    }
-}
-
-__global__ void k_step_advance(uint32_t* step) { *step += 1; }
-
-cudaError_t launch_argmax_pick(const void* logits, uint32_t B, uint32_t V, uint32_t* cur, uint32_t* history,
-                               uint32_t hist_stride, uint32_t* step, const void* embed, void* hidden, uint32_t d_model,
-                               cudaStream_t s) {
-    if (!B) return cudaSuccess;
-    k_argmax_pick<<<B, 1024, 0, s>>>(static_cast<const __half*>(logits), V, cur, history, hist_stride, step,
-                                     static_cast<const __half*>(embed), static_cast<__half*>(hidden), d_model);
-    if (step) k_step_advance<<<1, 1, 0, s>>>(step);
     return cudaGetLastError();
 }
 

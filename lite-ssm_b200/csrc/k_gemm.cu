@@ -28,9 +28,10 @@
 namespace lssm {
 
 // ---------------------------------------------------------------------------
-//  Tensor-map encoding through the driver entry point (no -lcuda link needed).
+//  Tensor-map encoding through the driver entry point (no -lcuda link needed); shared
+//  by every kernel file that builds tensor maps.
 // ---------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -47,7 +48,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // 2-D row-major [rows, cols] 16-bit matrix, box = [box_rows, 64 cols], 128-byte swizzle.
 bool make_tmap_2d_k64(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
                       uint32_t box_rows, CUtensorMapDataType dt) {
-    auto enc = get_encode_fn();
+    auto enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {row_stride_elems * 2};
@@ -183,7 +184,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 tc::tmem_ld32(tmem_base + acc * BN + ch * 32 + ((q * 32) << 16), v);
                 tc::tmem_ld_wait();
                 const uint32_t col0 = nb * BN + ch * 32;
-                if (row < M && col0 < N) {
+                if (row < M && col0 < N && epilogue == 3) {
+                    // fp32 output (partial sums that a collective adds before rounding)
+                    float* yf = reinterpret_cast<float*>(Y) + (uint64_t)row * ldy + col0;
+                    if (vec && col0 + 32 <= N && (ldy % 4 == 0)) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(yf)[j] = reinterpret_cast<uint4*>(v)[j];
+                    } else {
+                        for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) yf[j] = __uint_as_float(v[j]);
+                    }
+                } else if (row < M && col0 < N) {
                     __half h[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -248,6 +258,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __half* __restrict__ X,
             const uint32_t r = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
             if (r < M && c < N) {
                 float f = acc[i][j];
+                if (epilogue == 3) { reinterpret_cast<float*>(Y)[(uint64_t)r * N + c] = f; continue; }
                 if (epilogue == 1) f = silu(f);
                 Y[(uint64_t)r * N + c] = __float2half_rn(f);
             }

@@ -185,7 +185,16 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
                 tc::tmem_ld32(tmem_base + acc * BN + ch * 32 + ((q * 32) << 16), v);
                 tc::tmem_ld_wait();
                 const uint32_t col0 = nb * BN + ch * 32;
-                if (row < M && col0 < N) {
+                if (row < M && col0 < N && epilogue == 3) {
+                    // fp32 output (partial sums that a collective adds before rounding)
+                    float* yf = reinterpret_cast<float*>(Y) + (uint64_t)row * N + col0;
+                    if (vec && col0 + 32 <= N && (N % 4 == 0)) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(yf)[j] = reinterpret_cast<uint4*>(v)[j];
+                    } else {
+                        for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) yf[j] = __uint_as_float(v[j]);
+                    }
+                } else if (row < M && col0 < N) {
                     __half h[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -259,16 +268,8 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
 
 // [N rows][K/2 bytes] packed nibbles; box = BN rows x 32 bytes (one 64-wide K block).
 bool make_tmap_q(CUtensorMap* map, const void* base, uint32_t N, uint32_t K, uint32_t BN) {
-    static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
-    if (!enc) {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return false;
-        enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
     cuuint64_t dims[2] = {K / 2, N};
     cuuint64_t strides[1] = {K / 2};
     cuuint32_t box[2] = {I4_BK / 2, BN};

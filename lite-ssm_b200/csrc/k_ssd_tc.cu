@@ -400,22 +400,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
-
 // 3-D map over (cols, L, batch) of a 16-bit row-major activation with row stride `rs`.
 bool make_map3(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint64_t batch, uint64_t rs, bool bf16) {
-    auto enc = encode_fn();
+    auto enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[3] = {cols, L, batch};
     cuuint64_t strides[2] = {rs * 2, L * rs * 2};

@@ -3,6 +3,8 @@
 // launcher declarations each kernel file exports to the C-ABI layer.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -77,6 +79,10 @@ cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void
                                     cudaStream_t s);
 // INT4 GEMM with the dequantisation fused into the tcgen05 pipeline (k_gemm_i4.cu), same
 // fp16 rounding of each weight; cudaErrorNotSupported when K % 256 or alignment rule it out.
+// cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// One-time per-device setup of the GEMV kernels (shared-memory limits), from context creation.
+void gemv_init();
 cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
                            uint32_t K, int epilogue, cudaStream_t s);
 
@@ -148,5 +154,21 @@ size_t decode_persist_maps_bytes(uint32_t n_layer);
 // Encodes the 4 * n_layer + 1 tensor maps into host memory `out` (decode_persist_maps_bytes).
 bool decode_persist_encode_maps(void* out, const PLayer* layers, const void* lm_head, const PersistShape& sh,
                                 uint32_t seg_in, uint32_t seg_out, uint32_t seg_lm);
+
+// ---- head tensor parallelism (comm_nccl.cu, k_tp.cu) -------------------------
+lssm_status comm_allreduce_f32(lssm_comm* c, float* buf, size_t n, cudaStream_t s);
+lssm_status comm_allgather(lssm_comm* c, const void* src, void* dst, size_t bytes, cudaStream_t s);
+int comm_rank(const lssm_comm* c);
+int comm_world(const lssm_comm* c);
+cudaError_t launch_rowsumsq(const void* x, uint64_t stride, uint32_t rows, uint32_t dim, float* out, cudaStream_t s);
+cudaError_t launch_rmsnorm_total(const void* x, uint64_t stride, const void* w, const float* sumsq, uint32_t rows,
+                                 uint32_t dim, uint32_t dim_total, float eps, void* y, cudaStream_t s);
+cudaError_t launch_residual_f32(void* hidden, const float* part, uint64_t n, cudaStream_t s);
+uint32_t argmax_chunks(uint32_t Vr);
+cudaError_t launch_argmax_chunks(const void* logits, uint32_t ld, uint32_t B, uint32_t Vr, uint32_t v_off, uint2* cpair,
+                                 uint32_t* ticket, uint2* out, cudaStream_t s);
+cudaError_t launch_argmax_merge(const uint2* pairs, uint32_t world, uint32_t B, uint32_t* cur, uint32_t* history,
+                                uint32_t hist_stride, uint32_t* step, const void* embed, void* hidden, uint32_t d_model,
+                                cudaStream_t s);
 
 }  // namespace lssm

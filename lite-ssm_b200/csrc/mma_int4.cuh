@@ -1,6 +1,5 @@
-// mma_int4.cuh — register-operand INT4_B32 dequantisation + mma.sync helpers and
-// bulk (non-tensor) TMA copies, shared by the GEMV kernels and the persistent decode
-// kernel.
+// mma_int4.cuh — register-operand INT4_B32 dequantisation + mma.sync helpers, bulk and
+// tensor-map TMA copies, shared by the GEMV kernels and the persistent decode kernel.
 //
 // INT4_B32 nibble q for (row, k): byte row*(K/2) + k/2, low nibble = even k,
 // q = nib < 8 ? nib : nib - 16 (shaders/linear.metal:38-61). A 32-bit word holds 8
@@ -9,6 +8,7 @@
 // for the high nibble of each byte), one HSUB2 / HFMA2 removes the bias.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 
@@ -39,6 +39,22 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t q[4]) {
     q[1] = *reinterpret_cast<uint32_t*>(&h1);
     q[2] = *reinterpret_cast<uint32_t*>(&h2);
     q[3] = *reinterpret_cast<uint32_t*>(&h3);
+}
+
+// Bias-folding dequantisation: every nibble is moved to bits 4..7 of its fp16 lane
+// (w << 4, w, w >> 4, w >> 8) and one lop3 per pair writes (nib ^ 8) there under the
+// exponent of 64.0, giving the exact values 64 + u, u = nib ^ 8 = q + 8, in the pairs
+// (k0,k4) (k1,k5) (k2,k6) (k3,k7). A dot product with x over them equals
+// sum(q * x) + 72 * sum(x): the caller starts the MMA accumulator at -72 * sum(x) of
+// the block. 7 instructions per word (3 shifts + 4 lop3) instead of dequant_word's 9,
+// and the folded bias is only 72x the activation, so the fp32 accumulation keeps the
+// products' precision.
+__device__ __forceinline__ void dequant_word_fold(uint32_t w, uint32_t q[4]) {
+    const uint32_t HI = 0x00F000F0u, M64 = 0x54805480u;
+    q[0] = lop3_6a(w << 4, HI, M64);
+    q[1] = lop3_6a(w, HI, M64);
+    q[2] = lop3_6a(w >> 4, HI, M64);
+    q[3] = lop3_6a(w >> 8, HI, M64);
 }
 
 // D += A(16x16, f16) * B(16x8, f16), fp32 accumulate.
@@ -73,6 +89,29 @@ __device__ __forceinline__ bool bar_wait_bounded(uint32_t bar, uint32_t parity) 
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         if (t - t0 > 2000000000ull) return false;
     }
+}
+
+// L2 evict-first policy for weight streams read once per step.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                                     uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma2(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint32_t bar,
+                                     uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
+        : "memory");
 }
 
 }  // namespace lssm

@@ -113,6 +113,10 @@ _SIGS = {
     "lssm_model_tensor": [P, C.c_char_p, C.POINTER(u64), C.POINTER(u64), C.POINTER(u32)],
     "lssm_model_destroy": [P],
     "lssm_session_create": [P, P, u32, u32, C.POINTER(P)],
+    "lssm_session_create_tp": [P, P, P, u32, u32, C.POINTER(P)],
+    "lssm_comm_unique_id": [P],
+    "lssm_comm_init": [P, C.c_int, C.c_int, P, C.POINTER(P)],
+    "lssm_comm_destroy": [P],
     "lssm_session_destroy": [P],
     "lssm_session_reset": [P],
     "lssm_prefill": [P, P, u32, P],
@@ -129,6 +133,8 @@ _OTHER = {
     "lssm_version": (C.c_char_p, []),
     "lssm_backend_loaded": (C.c_int, []),
     "lssm_has_kernel": (C.c_int, [C.c_char_p]),
+    "lssm_comm_rank": (C.c_int, [P]),
+    "lssm_comm_world": (C.c_int, [P]),
     "lssm_batch_active": (C.c_int, [P]),
     "lssm_ctx_stream": (P, [P]),
     "lssm_model_nbytes": (sz, [P]),
@@ -427,16 +433,59 @@ class Model:
             pass
 
 
-class Session:
-    """Mamba2State + Mamba2Workspace for `batch` independent sequences."""
+COMM_ID_BYTES = 128
 
-    def __init__(self, ctx: Ctx, model: Model, batch: int, max_seq_len: int):
+
+class Comm:
+    """NCCL communicator of one rank (head tensor parallelism): rank 0 makes the id with
+    Comm.unique_id(), the caller shares it (e.g. torch.distributed broadcast), every rank
+    builds Comm(ctx, rank, world, uid)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * COMM_ID_BYTES)()
+        check(lib().lssm_comm_unique_id(C.cast(buf, P)))
+        return bytes(buf)
+
+    def __init__(self, ctx: Ctx, rank: int, world: int, uid: bytes):
+        if len(uid) != COMM_ID_BYTES:
+            raise ValueError(f"unique id must be {COMM_ID_BYTES} bytes")
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(uid)
+        h = P()
+        check(lib().lssm_comm_init(ctx.h, rank, world, C.cast(buf, P), C.byref(h)))
+        self.h = h
+        self.ctx = ctx
+        self.rank, self.world = rank, world
+        ctx._track(self)
+
+    def close(self):
+        if self.h:
+            lib().lssm_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """Mamba2State + Mamba2Workspace for `batch` independent sequences. With `comm`, a
+    head-tensor-parallel session over this rank's shard of the model (calls are then
+    collective: every rank runs them with the same tokens)."""
+
+    def __init__(self, ctx: Ctx, model: Model, batch: int, max_seq_len: int, comm: "Comm | None" = None):
         self.ctx = ctx
         self.model = model
         self.batch = batch
         self.vocab = model.config().vocab_size
+        self.comm = comm
         h = P()
-        check(lib().lssm_session_create(ctx.h, model.h, batch, max_seq_len, C.byref(h)))
+        if comm is None:
+            check(lib().lssm_session_create(ctx.h, model.h, batch, max_seq_len, C.byref(h)))
+        else:
+            check(lib().lssm_session_create_tp(ctx.h, model.h, comm.h, batch, max_seq_len, C.byref(h)))
         self.h = h
         ctx._track(self)
 
@@ -500,6 +549,31 @@ class Session:
             self.close()
         except Exception:
             pass
+
+
+def tp_shard_plan(hp: dict, rank: int, world: int) -> dict:
+    """Which model rows / columns rank `rank` of `world` holds under head tensor
+    parallelism (the layout lssm_session_create_tp copies): in_proj row segments
+    [z | x | B | C | dt], conv channel segments [x | B | C], the head slice, the d_inner
+    column slice of out_proj / mixer norm, and the lm_head vocab slice."""
+    H, G, P, N = hp["n_heads"], hp["n_groups"], hp["d_head"], hp["d_state"]
+    if H % world or G % world:
+        raise ValueError("n_heads and n_groups must divide by the world size")
+    di = hp["expand"] * hp["d_model"]
+    GN, Hr, Gr = G * N, H // world, G // world
+    dir_, GNr = Hr * P, Gr * N
+    xd = di + 2 * GN
+    V = hp["vocab_size"]
+    vmax = -(-V // world)
+    voff = min(V, rank * vmax)
+    return {
+        "in_rows": [(rank * dir_, dir_), (di + rank * dir_, dir_), (2 * di + rank * GNr, GNr),
+                    (2 * di + GN + rank * GNr, GNr), (di + xd + rank * Hr, Hr)],
+        "conv_channels": [(rank * dir_, dir_), (di + rank * GNr, GNr), (di + GN + rank * GNr, GNr)],
+        "heads": (rank * Hr, Hr),
+        "inner_cols": (rank * dir_, dir_),
+        "vocab": (voff, min(vmax, V - voff)),
+    }
 
 
 def hparams(**kw) -> HParams:

@@ -65,14 +65,16 @@ def test_graph_and_eager_decode_agree(ctx, golden):
     assert np.array_equal(outs[0][1], outs[1][1])
 
 
-def test_batched_sequences_match_single(ctx, golden):
+@pytest.mark.parametrize("nb", [3, 8])
+def test_batched_sequences_match_single(ctx, golden, nb):
+    """Batch rows 2..8 take the multi-row GEMV kernels (mma fp16 lm_head); batch 1 the single-row ones."""
     model = lssm.Model.load(ctx, golden / "tinyB_int4.ssm")
     rng = np.random.default_rng(3)
-    prompts = rng.integers(0, 288, size=(3, 21)).astype(np.uint32)
-    sb = lssm.Session(ctx, model, batch=3, max_seq_len=32)
+    prompts = rng.integers(0, 288, size=(nb, 21)).astype(np.uint32)
+    sb = lssm.Session(ctx, model, batch=nb, max_seq_len=32)
     batched = sb.generate(prompts, 9)
     lb = sb.logits()
-    for b in range(3):
+    for b in range(nb):
         s1 = lssm.Session(ctx, model, batch=1, max_seq_len=32)
         single = s1.generate(prompts[b:b + 1], 9)
         assert np.array_equal(single[0], batched[b])
@@ -100,6 +102,21 @@ def test_synthesized_model_generation_vs_oracle(ctx):
     ora = po.OracleModel(m.download_bytes(), mode=0)
     otoks, opre, ostep = ora.generate(prompt[0], 8, teacher=toks)
     assert near_tie_ok(toks, otoks, np.concatenate([opre[None], ostep]))
+
+
+def test_synthesized_batch4_vs_oracle(ctx):
+    """Batch-4 decode of a model whose in_proj (5288 rows) takes the streaming INT4 GEMV
+    and whose lm_head takes the multi-row fp16 MMA GEMV, each sequence against the oracle."""
+    hp = dict(d_model=1280, n_layer=2, d_state=64, d_conv=4, expand=2, vocab_size=512, n_heads=40, d_head=64,
+              chunk_size=64, n_groups=1, norm_before_gate=0)
+    m = lssm.Model.synthesize(ctx, lssm.hparams(**hp), seed=6, int4=True)
+    prompts = np.random.default_rng(10).integers(0, 512, size=(4, 40)).astype(np.uint32)
+    s = lssm.Session(ctx, m, batch=4, max_seq_len=40)
+    toks = s.generate(prompts, 6)
+    ora = po.OracleModel(m.download_bytes(), mode=0)
+    for b in range(4):
+        otoks, opre, ostep = ora.generate(prompts[b], 6, teacher=toks[b])
+        assert near_tie_ok(toks[b], otoks, np.concatenate([opre[None], ostep]))
 
 
 def test_engine_errors(ctx, golden):

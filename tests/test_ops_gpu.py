@@ -134,7 +134,10 @@ def _int4_weights(N, K, scale=0.05):
     return packed, scales
 
 
-@pytest.mark.parametrize("N,K,off", [(1000, 2560, 0), (77, 96, 0), (300, 5120, 0), (50, 64, 2)])
+# N >= 16 x SM count with K % 256 == 0 takes the streaming kernel (1 CTA per SM,
+# K chunks of 1024 / 512 / 256 through a shared-memory ring), the rest the per-tile ones
+@pytest.mark.parametrize("N,K,off", [(1000, 2560, 0), (77, 96, 0), (300, 5120, 0), (50, 64, 2), (10576, 2560, 0),
+                                     (2560, 5120, 0), (4813, 1280, 0), (3000, 8192, 0)])
 def test_linear_int4_gemv(ctx, ops, N, K, off):
     packed, scales = _int4_weights(N, K)
     x = h(RNG.standard_normal(K))
