@@ -435,25 +435,48 @@ def run_kernel_bench(args):
             N, K = 10576, 2560
         else:
             N, K = 2560, 5120
+        N, K = args.gemv_n or N, args.gemv_k or K
+        R = args.rows
         per = N * K // 2 + N * K // 16
         nl = 64
         W = torch.randint(0, 256, (nl * per,), dtype=torch.uint8, device=dev, generator=g)
         sc = (torch.rand((nl, N * K // 32), device=dev, generator=g) * 0.01 + 1e-3).half()
         Wv = W.view(nl, per)
         Wv[:, N * K // 2:] = sc.view(torch.uint8).view(nl, -1)
-        x = torch.randn(K, device=dev, generator=g).half()
-        y = torch.empty(N, device=dev, dtype=torch.half)
+        x = torch.randn(R, K, device=dev, generator=g).half()
+        y = torch.empty(R, N, device=dev, dtype=torch.half)
         torch.cuda.synchronize()
-        dims = lssm.LinearDims(1, N, K)
+        dims = lssm.LinearDims(R, N, K)
         base = W.data_ptr()
+        fn = L.lssm_linear_int4_gemv if R == 1 else L.lssm_linear_int4_gemv_rows
 
         def call(i):
             o = (i % nl) * per
-            lssm.check(L.lssm_linear_int4_gemv(ctx.h, x.data_ptr(), 0, base, o, base, o + N * K // 2, y.data_ptr(),
-                                               0, dims))
+            lssm.check(fn(ctx.h, x.data_ptr(), 0, base, o, base, o + N * K // 2, y.data_ptr(), 0, dims))
+        call(0)   # loads the kernel outside the graph capture
+        torch.cuda.synchronize()
         ms = timed(call, reps)
-        b = per + K * 2 + N * 2
-        out.update(shape=[N, K], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+        b = per + R * K * 2 + R * N * 2
+        out.update(shape=[R, N, K], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+    elif args.kernel == "f16_gemv":
+        N, K, R = args.gemv_n or 50288, args.gemv_k or 2560, args.rows
+        per = N * K * 2
+        nl = max(2, min(64, int(4e9 // per)))
+        W = (torch.randn(nl * N * K, device=dev, generator=g) * 0.05).half()
+        x = torch.randn(R, K, device=dev, generator=g).half()
+        y = torch.empty(R, N, device=dev, dtype=torch.half)
+        torch.cuda.synchronize()
+        dims = lssm.LinearDims(R, N, K)
+        base = W.data_ptr()
+        fn = L.lssm_linear_f16_gemv if R == 1 else L.lssm_linear_f16_gemv_rows
+
+        def call(i):
+            lssm.check(fn(ctx.h, x.data_ptr(), 0, base, (i % nl) * per, y.data_ptr(), 0, dims))
+        call(0)
+        torch.cuda.synchronize()
+        ms = timed(call, reps)
+        b = per + R * K * 2 + R * N * 2
+        out.update(shape=[R, N, K], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
     elif args.kernel in ("gemm_f16", "int4_gemm"):
         M, N, K = args.m, args.n, args.k
         X = torch.randn(M, K, device=dev, generator=g).half()
@@ -716,9 +739,13 @@ def main():
     ap.add_argument("--batched-prompt", type=int, default=512)
     ap.add_argument("--batched-new", type=int, default=256)
     ap.add_argument("--kernel", default=None,
-                    choices=["int4_gemv", "int4_gemv_out", "gemm_f16", "int4_gemm", "ssd_chunked", "ssd_step"],
+                    choices=["int4_gemv", "int4_gemv_out", "f16_gemv", "gemm_f16", "int4_gemm", "ssd_chunked",
+                             "ssd_step"],
                     help="single-kernel microbenchmark instead of the model bench")
     ap.add_argument("--reps", type=int, default=64)
+    ap.add_argument("--rows", type=int, default=1, help="activation rows of the GEMV microbenchmarks (1..8)")
+    ap.add_argument("--gemv-n", type=int, default=0, help="GEMV microbenchmark N (0: the 2.7B shape)")
+    ap.add_argument("--gemv-k", type=int, default=0, help="GEMV microbenchmark K (0: the 2.7B shape)")
     ap.add_argument("--m", type=int, default=2048)
     ap.add_argument("--n", type=int, default=10576)
     ap.add_argument("--k", type=int, default=2560)

@@ -127,6 +127,15 @@ lssm_status lssm_linear_int4_gemv(lssm_ctx* ctx, const void* x, size_t x_off, co
 lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:141-145 */
+/* Batched-decode extensions (no MetalOps counterpart): the GEMVs above take one activation
+ * row (dims.M == 1, the checks of ops.mm:207-212 and :323-324); these take 1 <= dims.M <= 8 rows
+ * (the sequences of one decode step, row-major (M, K) in, (M, N) out) and read the weights once
+ * for all rows. Same errors otherwise. */
+lssm_status lssm_linear_f16_gemv_rows(lssm_ctx* ctx, const void* x, size_t x_off, const void* w, size_t w_off,
+                                      void* y, size_t y_off, lssm_linear_dims dims);
+lssm_status lssm_linear_int4_gemv_rows(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
+                                       size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
+                                       size_t y_off, lssm_linear_dims dims);
 lssm_status lssm_silu_f16(lssm_ctx* ctx, const void* x, size_t x_off, void* y, size_t y_off,
                           uint32_t n);                                                  /* ops.hpp:147-149 */
 lssm_status lssm_add_inplace_f16(lssm_ctx* ctx, void* y, size_t y_off, const void* x, size_t x_off,
@@ -269,7 +278,11 @@ lssm_status lssm_session_set_option(lssm_session* s, const char* key, int64_t va
  * activations (the gated RMSNorm spans the full d_inner, mamba2_block.cpp:235-238) and
  * the fp32 out_proj partials, rounded to fp16 once before the residual add. lm_head
  * argmax merges the ranks' (value, index) pairs with the first-max rule. Requires
- * n_heads and n_groups divisible by the world size. */
+ * n_heads and n_groups divisible by the world size. Session creation is collective too.
+ * Decode steps run both all-reduces over a peer-memory exchange (CUDA IPC mappings of
+ * every rank's receive area, peer stores + release/acquire flags over NVLink, the residual
+ * add fused in) when all ranks are on distinct GPUs with peer access, else over NCCL;
+ * session option "tp_p2p" = 0 forces NCCL (set it alike on every rank). */
 #define LSSM_COMM_ID_BYTES 128
 typedef struct lssm_comm lssm_comm;
 /* NCCL unique id (LSSM_COMM_ID_BYTES bytes) made on one rank; the caller shares it. */
@@ -277,12 +290,20 @@ lssm_status lssm_comm_unique_id(uint8_t* out);
 lssm_status lssm_comm_init(lssm_ctx* ctx, int rank, int world, const uint8_t* id, lssm_comm** out);
 lssm_status lssm_comm_destroy(lssm_comm* c);
 int lssm_comm_rank(const lssm_comm* c);
+/* Sum-all-reduce of n fp32 device values in place across the ranks (collective, one-shot):
+ * the peer exchange for n <= 65536 when every rank can use it, else NCCL. */
+lssm_status lssm_comm_allreduce_f32(lssm_comm* c, float* buf, size_t n);
 int lssm_comm_world(const lssm_comm* c);
 /* A session over this rank's shard of `m` (see above). lssm_prefill / lssm_decode /
  * lssm_generate / lssm_session_logits are then collective: every rank calls them with the
  * same tokens. */
 lssm_status lssm_session_create_tp(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch,
                                    uint32_t max_seq_len, lssm_session** out);
+
+/* Failure-path check of the peer exchange on one GPU: runs the exchange kernel against
+ * local buffers with a flag no rank sets, so its bounded wait (spin_ns) runs out. Returns
+ * LSSM_ERR_TIMEOUT and leaves the context usable. */
+lssm_status lssm_p2p_wait_selftest(lssm_ctx* ctx, uint64_t spin_ns);
 
 /* Phase trace of the last persistent decode: sm_count x (n_layer * 10 + 6) u64 words.
  * Per layer: [0] layer start, [1] in_proj RMSNorm staged, [2] in_proj + conv done,

@@ -343,6 +343,24 @@ lssm_status lssm_linear_int4_gemv(lssm_ctx* ctx, const void* x, size_t x_off, co
                                                 bp(y, y_off), 1, d.N, d.K, ctx->stream));
 }
 
+lssm_status lssm_linear_f16_gemv_rows(lssm_ctx* ctx, const void* x, size_t x_off, const void* w, size_t w_off,
+                                      void* y, size_t y_off, lssm_linear_dims d) {
+    CHECK_CTX(ctx);
+    if (d.M < 1 || d.M > 8) return fail(LSSM_ERR_INVALID_ARGUMENT, "linear_f16_gemv_rows: M must be 1..8");
+    LAUNCH("linear_f16_gemv_rows", launch_gemv_f16(bp(x, x_off), bp(w, w_off), bp(y, y_off), d.M, d.N, d.K, nullptr,
+                                                   0.0f, 0, ctx->stream));
+}
+
+lssm_status lssm_linear_int4_gemv_rows(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
+                                       size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
+                                       size_t y_off, lssm_linear_dims d) {
+    CHECK_CTX(ctx);
+    if (d.M < 1 || d.M > 8) return fail(LSSM_ERR_INVALID_ARGUMENT, "linear_int4_gemv_rows: M must be 1..8");
+    if (d.K % 32 != 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "linear_int4_gemv_rows: K must be a multiple of 32");
+    LAUNCH("linear_int4_gemv_rows", launch_gemv_int4(bp(x, x_off), bp(w, w_packed_off), bp(w_scl, w_scales_off),
+                                                     bp(y, y_off), d.M, d.N, d.K, ctx->stream));
+}
+
 lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, const void* w, size_t w_packed_off,
                                   const void* w_scl, size_t w_scales_off, void* y, size_t y_off,
                                   lssm_linear_dims d) {

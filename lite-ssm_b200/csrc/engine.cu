@@ -520,6 +520,7 @@ struct lssm_session {
     // head tensor parallelism
     lssm_comm* comm = nullptr;
     int tp_rank = 0, tp_world = 1;
+    bool use_p2p = true;            // decode all-reduces over the peer exchange when it is set up
     uint8_t* d_shard = nullptr;
     float *d_sumsq = nullptr, *d_part32 = nullptr;
     __half* d_gather = nullptr;    // all ranks' logits, for lssm_session_logits
@@ -788,26 +789,16 @@ static lssm_status build_tp_shard(lssm_session* s) {
     return LSSM_OK;
 }
 
-static lssm_status session_create_impl(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch, uint32_t max_L,
-                                       lssm_session** out) {
-    if (!ctx || !m || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: null argument");
-    if (batch == 0 || max_L == 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: batch and max_seq_len must be >= 1");
-    cudaSetDevice(ctx->device);
-    *out = nullptr;
-    std::unique_ptr<lssm_session, lssm_status (*)(lssm_session*)> s(new lssm_session(), lssm_session_destroy);
-    s->ctx = ctx;
-    s->m = m;
-    s->batch = batch;
-    s->max_L = max_L;
+// Shard, buffers and options of a new session (no collective steps).
+static lssm_status session_alloc(lssm_session* s, uint32_t batch, uint32_t max_L) {
+    lssm_model* m = s->m;
+    lssm_ctx* ctx = s->ctx;
     const SsmHeader& h = m->img.hdr;
     lssm_status st;
-    s->comm = comm;
-    s->tp_rank = comm_rank(comm);
-    s->tp_world = comm_world(comm);
-    if (comm) {
-        if ((st = build_tp_shard(s.get()))) return st;
+    if (s->comm) {
+        if ((st = build_tp_shard(s))) return st;
     } else {
-        bind_model_refs(s.get());
+        bind_model_refs(s);
     }
     const size_t rows = (size_t)batch * max_L;
     s->conv_layer = (size_t)batch * s->xd * h.d_conv;
@@ -833,7 +824,7 @@ static lssm_status session_create_impl(lssm_ctx* ctx, lssm_model* m, lssm_comm* 
     SA(s->d_cur, (size_t)batch * 4, "session: current tokens");
     SA(s->d_step, 16, "session: step");
     SA(s->d_err, 16, "session: error word");
-    if (comm) {
+    if (s->comm) {
         SA(s->d_sumsq, rows * 4, "session: TP sum of squares");
         SA(s->d_part32, rows * h.d_model * 4, "session: TP out_proj partials");
     }
@@ -855,8 +846,42 @@ static lssm_status session_create_impl(lssm_ctx* ctx, lssm_model* m, lssm_comm* 
 #undef SA
     for (auto& e : s->ev) cudaEventCreate(&e);
     cudaMemsetAsync(s->d_err, 0, 16, ctx->stream);
-    if (!comm && (st = setup_persistent(s.get()))) return st;
-    if (comm) s->persist_why = "tensor-parallel session";
+    if (!s->comm && (st = setup_persistent(s))) return st;
+    if (s->comm) s->persist_why = "tensor-parallel session";
+    return LSSM_OK;
+}
+
+// Under tensor parallelism session creation is collective: every rank allocates, the ranks
+// agree on the outcome (so one rank's failure fails all of them instead of leaving the others
+// waiting), then set up the peer exchange of the decode all-reduces together.
+static lssm_status session_create_impl(lssm_ctx* ctx, lssm_model* m, lssm_comm* comm, uint32_t batch, uint32_t max_L,
+                                       lssm_session** out) {
+    if (!ctx || !m || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: null argument");
+    if (batch == 0 || max_L == 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_session_create: batch and max_seq_len must be >= 1");
+    cudaSetDevice(ctx->device);
+    *out = nullptr;
+    std::unique_ptr<lssm_session, lssm_status (*)(lssm_session*)> s(new lssm_session(), lssm_session_destroy);
+    s->ctx = ctx;
+    s->m = m;
+    s->batch = batch;
+    s->max_L = max_L;
+    s->comm = comm;
+    s->tp_rank = comm_rank(comm);
+    s->tp_world = comm_world(comm);
+    lssm_status st = session_alloc(s.get(), batch, max_L);
+    if (comm) {
+        const std::string why = st ? lssm_last_error() : std::string();
+        bool all = false;
+        if (lssm_status cst = comm_agree(comm, st == LSSM_OK, &all)) return cst;
+        if (!all) {
+            if (st) return fail(st, "%s", why.c_str());
+            return fail(LSSM_ERR_CUDA, "lssm_session_create_tp: another rank failed to create its session");
+        }
+        // the peer exchange of the decode all-reduces (batch x d_model floats)
+        if ((st = comm_p2p_setup(comm, (size_t)batch * m->img.hdr.d_model))) return st;
+    } else if (st) {
+        return st;
+    }
     if ((st = lssm_session_reset(s.get()))) return st;
     *out = s.release();
     return LSSM_OK;
@@ -902,6 +927,11 @@ extern "C" lssm_status lssm_session_set_option(lssm_session* s, const char* key,
     }
     if (std::strcmp(key, "cuda_graph") == 0) {
         s->use_graph = value != 0;
+        if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+        return LSSM_OK;
+    }
+    if (std::strcmp(key, "tp_p2p") == 0) {   // set alike on every rank
+        s->use_p2p = value != 0;
         if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
         return LSSM_OK;
     }
@@ -1010,7 +1040,16 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         s->nl += 3;
     }
     // 7+8+9. gated RMSNorm + out_proj + residual add into hidden
-    if (s->comm) {
+    if (s->comm && decode && s->use_p2p && comm_p2p(s->comm, (size_t)rows * dm)) {
+        // decode: the same two all-reduces over the peer exchange, the second one adding the
+        // rounded sum to the residual in the same kernel
+        CU(launch_rowsumsq(s->gated, di, rows, di, s->d_sumsq, st));
+        if ((r = comm_p2p_allreduce(s->comm, s->d_sumsq, rows, s->d_sumsq, nullptr, st))) return r;
+        CU(launch_rmsnorm_total(s->gated, di, lw.mixer_norm, s->d_sumsq, rows, di, m->d_inner, 1e-5f, s->mixn, st));
+        if ((r = linear(s, lw.out_w, lw.out_dt, s->mixn, s->d_part32, rows, dm, di, nullptr, 3, st))) return r;
+        if ((r = comm_p2p_allreduce(s->comm, s->d_part32, (size_t)rows * dm, nullptr, s->hidden, st))) return r;
+        s->nl += 4;
+    } else if (s->comm) {
         // the gated RMSNorm spans the full d_inner: all-reduce each row's sum of squares; the
         // out_proj partials of this rank's d_inner columns are summed in fp32 across the ranks
         // and rounded to fp16 once before the residual add

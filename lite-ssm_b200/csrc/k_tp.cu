@@ -21,6 +21,8 @@
 
 namespace lssm {
 
+int* tc_error_word();
+
 namespace {
 
 __global__ void k_rowsumsq(const __half* __restrict__ x, uint64_t stride, uint32_t rows, uint32_t dim,
@@ -158,6 +160,76 @@ __global__ void k_argmax_merge(const uint2* __restrict__ pairs, uint32_t world,
             hidden[(uint64_t)b * d_model + k] = embed[(uint64_t)pick * d_model + k];
 }
 
+// Peer-memory sum-all-reduce of n fp32 (n <= 1024 * P2P_BLOCKS) for the tensor-parallel
+// decode step; CTA b owns floats [1024 b, 1024 b + 1024). Every value travels as one 8-byte
+// word (epoch << 32 | float bits): the receiver polls its words until they carry the
+// current epoch, so data and readiness arrive in the same store and no fence or separate
+// flag is needed. Per call CTA b takes the next epoch e of its own counter (every rank runs
+// the same calls, so the epochs agree), writes its words into parity e & 1 of every peer's
+// receive area (peer stores over NVLink), then reads its peers' words here and sums the
+// values in rank order (the same order on every rank: identical results). Two parities
+// suffice: a rank reaches epoch e + 2 only after reading every peer's epoch e + 1 words,
+// which that peer writes after its epoch-e kernel, reads included, has finished.
+// Residual form (hidden): hidden = half(hidden + half(sum)), the out_proj residual of
+// mamba2_block.cpp:274-276; else out = sum (may alias part). Each poll is bounded by
+// spin_ns; a timeout sets *err (the host reports LSSM_ERR_TIMEOUT) and the value counts 0.
+__global__ void __launch_bounds__(256) k_p2p_allreduce(P2PPeers peers, const uint64_t* recv_local,
+                                                       uint32_t* __restrict__ epochs, int rank, int world, uint64_t cap,
+                                                       const float* part, uint32_t n, float* out,
+                                                       __half* __restrict__ hidden, uint64_t spin_ns,
+                                                       int* __restrict__ err) {
+    __shared__ uint32_t e_sh;
+    const uint32_t tid = threadIdx.x, blk = blockIdx.x;
+    if (tid == 0) e_sh = ++epochs[blk];
+    __syncthreads();
+    const uint32_t e = e_sh, par = e & 1;
+    const uint32_t lo = blk * 1024, hi = min(n, lo + 1024);
+    for (uint32_t i = lo + tid; i < hi; i += 256) {
+        const uint64_t w = ((uint64_t)e << 32) | __float_as_uint(part[i]);
+        for (int r = 0; r < world; ++r) {
+            if (r == rank) continue;
+            uint64_t* dst = peers.recv[r] + ((uint64_t)par * world + rank) * cap + i;
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+        }
+    }
+    for (uint32_t i = lo + tid; i < hi; i += 256) {
+        float acc = 0.0f;
+        for (int r = 0; r < world; ++r) {
+            float v;
+            if (r == rank) {
+                v = part[i];
+            } else {
+                const uint64_t* src = recv_local + ((uint64_t)par * world + r) * cap + i;
+                uint64_t w;
+                uint64_t t0 = 0;
+                for (uint32_t k = 0;; ++k) {
+                    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+                    if ((uint32_t)(w >> 32) == e) break;
+                    if ((k & 255) == 0) {
+                        uint64_t t;
+                        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                        if (k == 0) {
+                            t0 = t;
+                        } else if (t - t0 > spin_ns) {
+                            atomicExch(err, 1);
+                            w = 0;
+                            break;
+                        }
+                    }
+                }
+                v = __uint_as_float((uint32_t)w);
+            }
+            acc += v;
+        }
+        if (hidden) {
+            const float o = __half2float(__float2half_rn(acc));
+            hidden[i] = __float2half_rn(__half2float(hidden[i]) + o);
+        } else {
+            out[i] = acc;
+        }
+    }
+}
+
 __global__ void k_step_inc(uint32_t* step) { *step += 1; }
 
 }  // namespace
@@ -201,6 +273,17 @@ cudaError_t launch_argmax_merge(const uint2* pairs, uint32_t world, uint32_t B, 
     k_argmax_merge<<<B, 256, 0, s>>>(pairs, world, B, cur, history, hist_stride, step,
                                      static_cast<const __half*>(embed), static_cast<__half*>(hidden), d_model);
     if (step) k_step_inc<<<1, 1, 0, s>>>(step);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_allreduce(const P2PPeers& peers, const uint64_t* recv_local, uint32_t* epochs, int rank,
+                                 int world, size_t cap, const float* part, uint32_t n, float* out, __half* hidden,
+                                 uint64_t spin_ns, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    const uint32_t blocks = (n + 1023) / 1024;
+    if (blocks > P2P_BLOCKS || n > cap || world > P2P_MAX_RANKS) return cudaErrorInvalidValue;
+    k_p2p_allreduce<<<blocks, 256, 0, s>>>(peers, recv_local, epochs, rank, world, cap, part, n, out, hidden, spin_ns,
+                                           tc_error_word());
     return cudaGetLastError();
 }
 

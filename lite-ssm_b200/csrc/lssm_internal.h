@@ -164,6 +164,20 @@ cudaError_t launch_rowsumsq(const void* x, uint64_t stride, uint32_t rows, uint3
 cudaError_t launch_rmsnorm_total(const void* x, uint64_t stride, const void* w, const float* sumsq, uint32_t rows,
                                  uint32_t dim, uint32_t dim_total, float eps, void* y, cudaStream_t s);
 cudaError_t launch_residual_f32(void* hidden, const float* part, uint64_t n, cudaStream_t s);
+// Peer exchange of the tensor-parallel decode (comm_nccl.cu / k_tp.cu).
+constexpr int P2P_MAX_RANKS = 8;
+constexpr uint32_t P2P_BLOCKS = 64;       // CTAs (slices of 1024 floats) per exchange
+struct P2PPeers {
+    uint64_t* recv[P2P_MAX_RANKS];        // rank r's receive area [2][world][cap] words, as mapped here
+};
+lssm_status comm_p2p_setup(lssm_comm* c, size_t floats);
+lssm_status comm_agree(lssm_comm* c, bool ok_local, bool* ok_all);
+bool comm_p2p(const lssm_comm* c, size_t floats);
+lssm_status comm_p2p_allreduce(lssm_comm* c, const float* part, size_t n, float* out, __half* hidden,
+                               cudaStream_t s);
+cudaError_t launch_p2p_allreduce(const P2PPeers& peers, const uint64_t* recv_local, uint32_t* epochs, int rank,
+                                 int world, size_t cap, const float* part, uint32_t n, float* out, __half* hidden,
+                                 uint64_t spin_ns, cudaStream_t s);
 uint32_t argmax_chunks(uint32_t Vr);
 cudaError_t launch_argmax_chunks(const void* logits, uint32_t ld, uint32_t B, uint32_t Vr, uint32_t v_off, uint2* cpair,
                                  uint32_t* ticket, uint2* out, cudaStream_t s);

@@ -92,6 +92,8 @@ _SIGS = {
     "lssm_linear_f16_gemm": [P, P, sz, P, sz, P, sz, LinearDims],
     "lssm_linear_silu_f16_gemm": [P, P, sz, P, sz, P, sz, LinearDims],
     "lssm_linear_int4_gemv": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
+    "lssm_linear_int4_gemv_rows": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
+    "lssm_linear_f16_gemv_rows": [P, P, sz, P, sz, P, sz, LinearDims],
     "lssm_linear_int4_gemm": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
     "lssm_silu_f16": [P, P, sz, P, sz, u32],
     "lssm_add_inplace_f16": [P, P, sz, P, sz, u32],
@@ -117,6 +119,8 @@ _SIGS = {
     "lssm_comm_unique_id": [P],
     "lssm_comm_init": [P, C.c_int, C.c_int, P, C.POINTER(P)],
     "lssm_comm_destroy": [P],
+    "lssm_p2p_wait_selftest": [P, u64],
+    "lssm_comm_allreduce_f32": [P, P, sz],
     "lssm_session_destroy": [P],
     "lssm_session_reset": [P],
     "lssm_prefill": [P, P, u32, P],
@@ -321,6 +325,15 @@ class Ops:
     def linear_int4_gemv(self, x, w_packed, w_scales, y, dims: LinearDims):
         self._call("lssm_linear_int4_gemv", *self._b(x), *self._b(w_packed), *self._b(w_scales), *self._b(y), dims)
 
+    def linear_int4_gemv_rows(self, x, w_packed, w_scales, y, dims: LinearDims):
+        """Batched-decode extension: 1..8 activation rows, weights read once."""
+        self._call("lssm_linear_int4_gemv_rows", *self._b(x), *self._b(w_packed), *self._b(w_scales), *self._b(y),
+                   dims)
+
+    def linear_f16_gemv_rows(self, x, w, y, dims: LinearDims):
+        """Batched-decode extension: 1..8 activation rows, weights read once."""
+        self._call("lssm_linear_f16_gemv_rows", *self._b(x), *self._b(w), *self._b(y), dims)
+
     def linear_int4_gemm(self, x, w_packed, w_scales, y, dims: LinearDims):
         self._call("lssm_linear_int4_gemm", *self._b(x), *self._b(w_packed), *self._b(w_scales), *self._b(y), dims)
 
@@ -457,6 +470,10 @@ class Comm:
         self.ctx = ctx
         self.rank, self.world = rank, world
         ctx._track(self)
+
+    def allreduce_f32(self, ptr: int, n: int):
+        """Sum n fp32 device values at ptr in place across the ranks (collective)."""
+        check(lib().lssm_comm_allreduce_f32(self.h, ptr, n))
 
     def close(self):
         if self.h:

@@ -150,6 +150,32 @@ def test_linear_int4_gemv(ctx, ops, N, K, off):
     close(get16(by, N), po.to_f32(ref))
 
 
+# batched-decode extension: rows 2..8; N >= 16 x SM count takes the streaming kernel
+@pytest.mark.parametrize("M,N,K", [(2, 300, 5120), (4, 4813, 1280), (8, 3000, 8192), (3, 18560, 4096)])
+def test_linear_int4_gemv_rows(ctx, ops, M, N, K):
+    packed, scales = _int4_weights(N, K)
+    x = h(RNG.standard_normal((M, K)))
+    ref = np.zeros(M * N, np.uint16)
+    po.lib().lssm_oracle_linear_int4(po.ptr(x.view(np.uint16)), po.ptr(packed), po.ptr(scales), po.ptr(ref), M, N, K,
+                                     0)
+    blob = np.concatenate([packed.ravel(), scales.view(np.uint8).ravel()])
+    bw, bx, by = hb(ctx, blob), hb(ctx, x), lssm.DeviceBuffer(ctx, M * N * 2)
+    ops.linear_int4_gemv_rows((bx, 0), (bw, 0), (bw, N * K // 2), (by, 0), lssm.LinearDims(M, N, K))
+    close(get16(by, M * N), po.to_f32(ref))
+    with pytest.raises(lssm.LssmError, match="M must be 1..8"):
+        ops.linear_int4_gemv_rows((bx, 0), (bw, 0), (bw, N * K // 2), (by, 0), lssm.LinearDims(9, N, K))
+
+
+@pytest.mark.parametrize("M,N,K", [(2, 1000, 2560), (5, 5000, 4096), (8, 777, 1024)])
+def test_linear_f16_gemv_rows(ctx, ops, M, N, K):
+    x = h(RNG.standard_normal((M, K)))
+    w = h(RNG.standard_normal((N, K)) * 0.05)
+    ref = x.astype(np.float32) @ w.astype(np.float32).T
+    bx, bw, by = hb(ctx, x), hb(ctx, w), lssm.DeviceBuffer(ctx, M * N * 2)
+    ops.linear_f16_gemv_rows((bx, 0), (bw, 0), (by, 0), lssm.LinearDims(M, N, K))
+    close(get16(by, M * N).reshape(M, N), ref, rtol=1e-2, atol=2e-3)
+
+
 def test_int4_rejects_bad_dims(ctx, ops):
     b = lssm.DeviceBuffer(ctx, 4096)
     with pytest.raises(lssm.LssmError, match="K must be a multiple of 32"):
