@@ -691,8 +691,9 @@ int* tc_error_word();
 //  (KC = 256 * segl k) of one tile, brought by two tensor-map copies issued by warp 7:
 //  the packed rows viewed as [K/256 lines][N rows][128 B] (box segl x 16 x 128 B,
 //  128-byte swizzle, so smem line = s * 16 + r and the 8 rows an MMA fragment reads
-//  fall in 8 different swizzle phases: conflict-free) and the scales [N][K/32] (box
-//  16 x KC/32). Warps 0..6 split the chunk's 32-k blocks, run the exact dequant +
+//  fall in 8 different swizzle phases: conflict-free) and the scales viewed the same
+//  way as [K/256 lines][N rows][8 scales] (box segl x 16 x 16 B: a row's scales of one
+//  line are 16 B from the next row's, so the 8 rows' scale reads hit 8 bank groups). Warps 0..6 split the chunk's 32-k blocks, run the exact dequant +
 //  m16n8k16 MMA of k_gemv_int4_tma, release the stage (empty barrier, 7 arrivals) and
 //  at the end of a tile reduce their partials through a double-buffered shared array
 //  (one named barrier per tile). Up to nst stages are in flight per SM.
@@ -754,7 +755,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
         const uint32_t st = smem_u32(ring + (size_t)slot * stage_bytes);
         st_mbar_expect(fb, wbytes + 16 * sc_bytes);
         tma3(st, &wmap, 0, (int32_t)(t * 16), (int32_t)(ch * segl), fb, pol);
-        tma2(st + wbytes, &smap, (int32_t)(ch * KC / 32), (int32_t)(t * 16), fb, pol);
+        tma3(st + wbytes, &smap, 0, (int32_t)(t * 16), (int32_t)(ch * segl), fb, pol);
     };
     uint32_t issued = 0;
     uint64_t pol = 0;
@@ -810,8 +811,9 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
                 // block b: line s = b / 8, 16-byte chunk j = b % 8, swizzled by the row's phase g & 7
                 const uint8_t* wa_base = st + g * 128 + 4 * c;
                 const uint8_t* wb_base = wa_base + 8 * 128;
-                const __half* sa = reinterpret_cast<const __half*>(st + wbytes + g * sc_bytes);
-                const __half* sb = reinterpret_cast<const __half*>(st + wbytes + (g + 8) * sc_bytes);
+                // scale of (row r, block b): [b / 8][r][b % 8]
+                const __half* sa = reinterpret_cast<const __half*>(st + wbytes + g * 16);
+                const __half* sb = sa + 8 * 8;
                 const uint32_t gb0 = ch * nbc;
                 const uint4* xc = xrow + (uint64_t)gb0 * 4;
                 const float2* cc = corr2 + (uint64_t)gb0 * 4;
@@ -832,7 +834,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
                     const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
                     mma_16816(d, a1, xf.x, xf.y);
                     mma_16816(d, a2, xf.z, xf.w);
-                    const float fa = __half2float(sa[b]), fb = __half2float(sb[b]);
+                    const uint32_t so = (b >> 3) * 128 + (b & 7);
+                    const float fa = __half2float(sa[so]), fb = __half2float(sb[so]);
                     acc[0] += d[0] * fa;
                     acc[1] += d[1] * fa;
                     acc[2] += d[2] * fb;
@@ -859,8 +862,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
 }
 
 // Tensor maps of one INT4_B32 matrix for k_gemv_int4_stream: packed rows as
-// [K/256 lines][N rows][128 B] (box segl x 16 x 128, 128-byte swizzle) and scales
-// [N][K/32] fp16 (box 16 x 8*segl).
+// [K/256 lines][N rows][128 B] (box segl x 16 x 128, 128-byte swizzle) and scales as
+// [K/256 lines][N rows][8 fp16] (box segl x 16 x 8).
 static bool stream_maps(CUtensorMap* wm, CUtensorMap* sm, const void* packed, const void* scales, uint32_t N,
                         uint32_t K, uint32_t segl) {
     auto enc = tensor_map_encoder();
@@ -873,10 +876,10 @@ static bool stream_maps(CUtensorMap* wm, CUtensorMap* sm, const void* packed, co
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
-    cuuint64_t sd[2] = {K / 32, N};
-    cuuint64_t ss[1] = {K / 32 * 2};
-    cuuint32_t sbox[2] = {8 * segl, 16};
-    return enc(sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(scales), sd, ss, sbox, one,
+    cuuint64_t sd[3] = {8, N, K / 256};
+    cuuint64_t ss[2] = {K / 32 * 2, 16};
+    cuuint32_t sbox[3] = {8, 16, segl};
+    return enc(sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(scales), sd, ss, sbox, one,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

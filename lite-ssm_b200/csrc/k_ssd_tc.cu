@@ -14,6 +14,9 @@
 //   MMA 2    Y  = M X + C' S_old                    (128x64, K = 128 + 128)
 //            S += B~^T X                            (128x64, K = 128)
 //   epilogue y_t = Y_t + D x_t -> global (f16 / bf16 / f32).
+// Pipelining: Y is double-buffered in TMEM and the per-chunk scalars (DT, Lc, W, EL) in
+// shared memory, so while the tensor cores run chunk c's MMA 2, the threads write chunk
+// c - 1's epilogue and warp 0 scans chunk c + 1's dt.
 // Math: the same recurrence as the reference (exp of segment sums, softplus-inside,
 // dt clamp); only the order of accumulation differs. M, C' and S_old are rounded to the
 // input dtype as MMA operands (the reference stores M and S as fp16, ssd_chunked.metal:116/121).
@@ -39,12 +42,12 @@ constexpr uint32_t OFF_C = OFF_X + 2 * X_BYTES;
 constexpr uint32_t OFF_B = OFF_C + 2 * BC_BYTES;
 constexpr uint32_t OFF_M = OFF_B + 2 * BC_BYTES;
 constexpr uint32_t OFF_S = OFF_M + BC_BYTES;
-constexpr uint32_t OFF_F = OFF_S + TN * TP * 2;     // DT, Lc, W, EL (4 x 128 floats)
-constexpr uint32_t OFF_BAR = OFF_F + 4 * TQ * 4;
+constexpr uint32_t OFF_F = OFF_S + TN * TP * 2;     // 2 chunks x {DT, Lc, W, EL} (128 floats each)
+constexpr uint32_t OFF_BAR = OFF_F + 8 * TQ * 4;
 constexpr uint32_t SMEM_TOTAL = OFF_BAR + 64 + 1024;
 constexpr uint32_t STAGE_TX = X_BYTES + 2 * BC_BYTES;
-// TMEM columns
-constexpr uint32_t T_CB = 0, T_Y = 128, T_S = 192, TMEM_COLS = 256;
+// TMEM columns: CB, two Y buffers (chunk parity), S
+constexpr uint32_t T_CB = 0, T_Y = 128, T_S = 256, TMEM_COLS = 512;
 
 struct TcArgs {
     const void* dt_raw; const void* dt_bias; const void* A_log; const void* D;
@@ -124,10 +127,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                      const __grid_constant__ CUtensorMap tmC, TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* DT = reinterpret_cast<float*>(sm + OFF_F);
-    float* Lc = DT + TQ;
-    float* Wj = Lc + TQ;
-    float* EL = Wj + TQ;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);   // full[0], full[1], cb, y
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -214,42 +213,87 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     if (warp == 0) load_dt(0, dnext);
 
+    // dt of chunk c -> softplus/clamp, cumulative log decay into scalar buffer c & 1 (warp 0)
+    auto scan_dt = [&](uint32_t c) {
+        float* F = reinterpret_cast<float*>(sm + OFF_F) + (c & 1) * 4 * TQ;
+        float d[4], run = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float v = 0.0f;
+            if (dnext[i] > -1e29f) v = fminf(fmaxf(softplus(dnext[i] + dbias), a.dt_min), a.dt_max);
+            d[i] = v;
+            run += A * v;
+        }
+        if (c + 1 < nc) load_dt(c + 1, dnext);
+        float incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float u = __shfl_up_sync(0xffffffffu, incl, o);
+            if ((int)lane >= o) incl += u;
+        }
+        float pre = incl - run;
+        const float lend = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t tt = lane * 4 + i;
+            pre += A * d[i];
+            F[tt] = d[i];
+            F[TQ + tt] = pre;
+            F[2 * TQ + tt] = __expf(lend - pre) * d[i];
+            F[3 * TQ + tt] = __expf(pre);
+        }
+    };
+    // y_t = Y_t + D x_t for chunk c (columns hc*32 .. +32), Y from TMEM buffer c & 1
+    auto epilogue = [&](uint32_t c, const uint32_t (&xr)[16]) {
+        const uint32_t t0 = c * TQ, tl = min((uint32_t)TQ, a.L - t0);
+        uint32_t v[32];
+        tc::tmem_ld32(tmem + lane_base + T_Y + (c & 1) * 64 + hc * 32, v);
+        tc::tmem_ld_wait();
+        if (t < tl) {
+            float y[32];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float2 xv = unpack2<BF16>(xr[e]);
+                y[2 * e] = __uint_as_float(v[2 * e]) + Dh * xv.x;
+                y[2 * e + 1] = __uint_as_float(v[2 * e + 1]) + Dh * xv.y;
+            }
+            const uint64_t o = ((uint64_t)b * a.L + t0 + t) * a.y_rs + (uint64_t)h * TP + hc * 32;
+            if (a.y_dtype == 2) {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.Y) + o);
+#pragma unroll
+                for (int qq = 0; qq < 8; ++qq)
+                    dst[qq] = make_float4(y[4 * qq], y[4 * qq + 1], y[4 * qq + 2], y[4 * qq + 3]);
+            } else {
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                    uint4 u;
+                    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        w[e] = (a.y_dtype == 1) ? pack2<true>(y[qq * 8 + 2 * e], y[qq * 8 + 2 * e + 1])
+                                                : pack2<false>(y[qq * 8 + 2 * e], y[qq * 8 + 2 * e + 1]);
+                    dst[qq] = u;
+                }
+            }
+        }
+    };
+    if (warp == 0) scan_dt(0);
+    uint32_t xprev[16];   // x rows of the chunk whose epilogue is pending
+#pragma unroll
+    for (int e = 0; e < 16; ++e) xprev[e] = 0;
+
     for (uint32_t c = 0; c < nc && ok; ++c) {
         const uint32_t buf = c & 1;
-        const uint32_t t0 = c * TQ, tl = min((uint32_t)TQ, a.L - t0);
         uint8_t* sX = sm + OFF_X + buf * X_BYTES;
         uint8_t* sC = sm + OFF_C + buf * BC_BYTES;
         uint8_t* sB = sm + OFF_B + buf * BC_BYTES;
-        // -- dt -> softplus/clamp, cumulative log decay (warp 0); prefetch next chunk's dt
-        if (warp == 0) {
-            float d[4], run = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float v = 0.0f;
-                if (dnext[i] > -1e29f) v = fminf(fmaxf(softplus(dnext[i] + dbias), a.dt_min), a.dt_max);
-                d[i] = v;
-                run += A * v;
-            }
-            if (c + 1 < nc) load_dt(c + 1, dnext);
-            float incl = run;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float u = __shfl_up_sync(0xffffffffu, incl, o);
-                if ((int)lane >= o) incl += u;
-            }
-            float pre = incl - run;
-            const float lend = __shfl_sync(0xffffffffu, incl, 31);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t tt = lane * 4 + i;
-                pre += A * d[i];
-                DT[tt] = d[i];
-                Lc[tt] = pre;
-                Wj[tt] = __expf(lend - pre) * d[i];
-                EL[tt] = __expf(pre);
-            }
-        }
-        __syncthreads();
+        const float* F = reinterpret_cast<const float*>(sm + OFF_F) + buf * 4 * TQ;
+        const float* DT = F;
+        const float* Lc = F + TQ;
+        const float* Wj = F + 2 * TQ;
+        const float* EL = F + 3 * TQ;
+        __syncthreads();   // scalars of chunk c visible
         // tiles of chunk c visible to every thread, and CB(c) done
         if (!tc::mbar_wait(smem_u32(&bars[buf]), (c >> 1) & 1, abort_flag)) { ok = false; break; }
         if (!tc::mbar_wait(bar_cb, c & 1, abort_flag)) { ok = false; break; }
@@ -309,18 +353,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_proxy_async_shared();
         tc::tc_fence_before();
         __syncthreads();
-        // -- Y = M X + C' S_old ; S += B~^T X ; then CB(c+1) so it overlaps this epilogue
+        // -- Y(c) = M X + C' S_old into TMEM buffer c & 1 ; S += B~^T X ; then CB(c+1)
         if (tid == 0) {
             tc::tc_fence_after();
             const uint32_t sMa = smem_u32(sm + OFF_M), sXa = smem_u32(sX), sSa = smem_u32(sm + OFF_S);
             const uint32_t sCa = smem_u32(sC), sBa = smem_u32(sB);
+            const uint32_t ty = tmem + T_Y + buf * 64;
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
-                tc::umma_f16(tmem + T_Y, tc::sw128_desc(sMa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
+                tc::umma_f16(ty, tc::sw128_desc(sMa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
                              tc::sw128_desc(sXa + k * 2048, PANEL, 1024), ID_Y, k > 0);
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
-                tc::umma_f16(tmem + T_Y, tc::sw128_desc(sCa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
+                tc::umma_f16(ty, tc::sw128_desc(sCa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
                              tc::sw128_desc(sSa + k * 2048, PANEL, 1024), ID_Y, 1);
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
@@ -331,6 +376,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (tc::mbar_wait(smem_u32(&bars[(c + 1) & 1]), ((c + 1) >> 1) & 1, abort_flag)) issue_cb(c + 1);
             }
         }
+        // -- while MMA 2 (c) runs: chunk c+1's dt scan, chunk c-1's epilogue
+        if (warp == 0 && c + 1 < nc) scan_dt(c + 1);
+        if (c > 0) epilogue(c - 1, xprev);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) xprev[e] = xreg[e];
         if (!tc::mbar_wait(bar_y, c & 1, abort_flag)) { ok = false; break; }
         tc::tc_fence_after();
         // this chunk's buffer is free now: prefetch chunk c + 2 into it
@@ -338,42 +388,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             issue_chunk(c + 2);
             last_issued = c + 2;
         }
-        // -- epilogue: y_t = Y_t + D x_t (columns hc*32 .. +32)
-        {
-            uint32_t v[32];
-            tc::tmem_ld32(tmem + lane_base + T_Y + hc * 32, v);
-            tc::tmem_ld_wait();
-            if (t < tl) {
-                float y[32];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float2 xv = unpack2<BF16>(xreg[e]);
-                    y[2 * e] = __uint_as_float(v[2 * e]) + Dh * xv.x;
-                    y[2 * e + 1] = __uint_as_float(v[2 * e + 1]) + Dh * xv.y;
-                }
-                const uint64_t o = ((uint64_t)b * a.L + t0 + t) * a.y_rs + (uint64_t)h * TP + hc * 32;
-                if (a.y_dtype == 2) {
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.Y) + o);
-#pragma unroll
-                    for (int qq = 0; qq < 8; ++qq)
-                        dst[qq] = make_float4(y[4 * qq], y[4 * qq + 1], y[4 * qq + 2], y[4 * qq + 3]);
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) {
-                        uint4 u;
-                        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            w[e] = (a.y_dtype == 1) ? pack2<true>(y[qq * 8 + 2 * e], y[qq * 8 + 2 * e + 1])
-                                                    : pack2<false>(y[qq * 8 + 2 * e], y[qq * 8 + 2 * e + 1]);
-                        dst[qq] = u;
-                    }
-                }
-            }
-        }
         tc::tc_fence_before();
-        __syncthreads();
+    }
+    if (ok && !*abort_flag && nc > 0) {
+        tc::tc_fence_after();
+        epilogue(nc - 1, xprev);
     }
 
     if (ok && !*abort_flag) {   // final state -> global
