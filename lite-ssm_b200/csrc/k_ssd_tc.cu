@@ -8,12 +8,14 @@
 //            double buffered: chunk c+1 loads while chunk c computes);
 //   scan     dt -> softplus + clamp, Lc = inclusive cumsum of A dt (one warp);
 //   MMA 1    CB = C_c B_c^T                         (128x128x128, TMEM)
-//   threads  M[t,j] = CB[t,j] exp(Lc_t - Lc_j) dt_j for j <= t, else 0 -> smem (K-major)
-//            C'_t = exp(Lc_t) C_t (in place), B~_j = exp(Lc_end - Lc_j) dt_j B_j (in place),
+//   threads  M[t,j] = CB[t,j] exp(Lc_t - Lc_j) dt_j for j <= t, else 0 -> smem (K-major),
+//            as CB * 2^(Lc_t log2 e - q_j) with q_j = Lc_j log2 e - log2 dt_j per column;
+//            B~_j = exp(Lc_end - Lc_j) dt_j B_j (in place),
 //            S_old -> 16-bit smem operand, S <- exp(Lc_end) S in TMEM
-//   MMA 2    Y  = M X + C' S_old                    (128x64, K = 128 + 128)
+//   MMA 2    Y  = M X                               (128x64, K = 128)
+//            CS = C S_old                           (128x64, K = 128)
 //            S += B~^T X                            (128x64, K = 128)
-//   epilogue y_t = Y_t + D x_t -> global (f16 / bf16 / f32).
+//   epilogue y_t = Y_t + exp(Lc_t) CS_t + D x_t -> global (f16 / bf16 / f32).
 // Pipelining: Y is double-buffered in TMEM and the per-chunk scalars (DT, Lc, W, EL) in
 // shared memory, so while the tensor cores run chunk c's MMA 2, the threads write chunk
 // c - 1's epilogue and warp 0 scans chunk c + 1's dt.
@@ -46,8 +48,8 @@ constexpr uint32_t OFF_F = OFF_S + TN * TP * 2;     // 2 chunks x {DT, Lc, W, EL
 constexpr uint32_t OFF_BAR = OFF_F + 8 * TQ * 4;
 constexpr uint32_t SMEM_TOTAL = OFF_BAR + 64 + 1024;
 constexpr uint32_t STAGE_TX = X_BYTES + 2 * BC_BYTES;
-// TMEM columns: CB, two Y buffers (chunk parity), S
-constexpr uint32_t T_CB = 0, T_Y = 128, T_S = 256, TMEM_COLS = 512;
+// TMEM columns: CB, two Y = M X buffers and two CS = C S_old buffers (chunk parity), S
+constexpr uint32_t T_CB = 0, T_Y = 128, T_CS = 256, T_S = 384, TMEM_COLS = 512;
 
 struct TcArgs {
     const void* dt_raw; const void* dt_bias; const void* A_log; const void* D;
@@ -64,6 +66,15 @@ struct TcArgs {
 __device__ __forceinline__ uint32_t sw_off(uint32_t row, uint32_t col) {
     const uint32_t panel = col >> 6, c = col & 63;
     return panel * PANEL + row * 128 + ((((c >> 3) ^ (row & 7)) & 7) << 4) + (c & 7) * 2;
+}
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+// 2^x with the PTX ex2.approx instruction (the same approximation __expf rests on).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 template <bool BF16>
@@ -237,25 +248,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < 4; ++i) {
             const uint32_t tt = lane * 4 + i;
             pre += A * d[i];
-            F[tt] = d[i];
+            F[tt] = pre * LOG2E - __log2f(fmaxf(d[i], 1e-30f));   // q_j (padding rows: masked anyway)
             F[TQ + tt] = pre;
             F[2 * TQ + tt] = __expf(lend - pre) * d[i];
             F[3 * TQ + tt] = __expf(pre);
         }
     };
-    // y_t = Y_t + D x_t for chunk c (columns hc*32 .. +32), Y from TMEM buffer c & 1
-    auto epilogue = [&](uint32_t c, const uint32_t (&xr)[16]) {
+    // y_t = Y_t + exp(Lc_t) CS_t + D x_t for chunk c (columns hc*32 .. +32), Y and CS from
+    // TMEM buffers c & 1; el = exp(Lc_t) of this thread's row
+    auto epilogue = [&](uint32_t c, const uint32_t (&xr)[16], float el) {
         const uint32_t t0 = c * TQ, tl = min((uint32_t)TQ, a.L - t0);
-        uint32_t v[32];
+        uint32_t v[32], w[32];
         tc::tmem_ld32(tmem + lane_base + T_Y + (c & 1) * 64 + hc * 32, v);
+        tc::tmem_ld32(tmem + lane_base + T_CS + (c & 1) * 64 + hc * 32, w);
         tc::tmem_ld_wait();
         if (t < tl) {
             float y[32];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float2 xv = unpack2<BF16>(xr[e]);
-                y[2 * e] = __uint_as_float(v[2 * e]) + Dh * xv.x;
-                y[2 * e + 1] = __uint_as_float(v[2 * e + 1]) + Dh * xv.y;
+                y[2 * e] = __uint_as_float(v[2 * e]) + el * __uint_as_float(w[2 * e]) + Dh * xv.x;
+                y[2 * e + 1] = __uint_as_float(v[2 * e + 1]) + el * __uint_as_float(w[2 * e + 1]) + Dh * xv.y;
             }
             const uint64_t o = ((uint64_t)b * a.L + t0 + t) * a.y_rs + (uint64_t)h * TP + hc * 32;
             if (a.y_dtype == 2) {
@@ -280,6 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     if (warp == 0) scan_dt(0);
     uint32_t xprev[16];   // x rows of the chunk whose epilogue is pending
+    float elprev = 0.0f;  // and its exp(Lc_t)
 #pragma unroll
     for (int e = 0; e < 16; ++e) xprev[e] = 0;
 
@@ -289,7 +303,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t* sC = sm + OFF_C + buf * BC_BYTES;
         uint8_t* sB = sm + OFF_B + buf * BC_BYTES;
         const float* F = reinterpret_cast<const float*>(sm + OFF_F) + buf * 4 * TQ;
-        const float* DT = F;
+        const float* Qj = F;
         const float* Lc = F + TQ;
         const float* Wj = F + 2 * TQ;
         const float* EL = F + 3 * TQ;
@@ -300,8 +314,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tc_fence_after();
         const float lend = Lc[TQ - 1];
         uint32_t xreg[16];   // x_t[hc*32 .. +32] packed, kept for the epilogue
+        const float elcur = EL[t];
         {
-            const float lct = Lc[t];
+            const float lct2 = Lc[t] * LOG2E;
             uint8_t* sM = sm + OFF_M;
 #pragma unroll 1
             for (uint32_t jc = 0; jc < 2; ++jc) {
@@ -317,8 +332,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int e = 0; e < 4; ++e) {
                         const uint32_t j0 = col0 + qq * 8 + e * 2;
                         float m0 = 0.0f, m1 = 0.0f;
-                        if (j0 <= t) m0 = __uint_as_float(v[qq * 8 + e * 2]) * __expf(lct - Lc[j0]) * DT[j0];
-                        if (j0 + 1 <= t) m1 = __uint_as_float(v[qq * 8 + e * 2 + 1]) * __expf(lct - Lc[j0 + 1]) * DT[j0 + 1];
+                        if (j0 <= t) m0 = __uint_as_float(v[qq * 8 + e * 2]) * ex2_approx(lct2 - Qj[j0]);
+                        if (j0 + 1 <= t) m1 = __uint_as_float(v[qq * 8 + e * 2 + 1]) * ex2_approx(lct2 - Qj[j0 + 1]);
                         w[e] = pack2<BF16>(m0, m1);
                     }
                     *reinterpret_cast<uint4*>(sM + sw_off(t, col0 + qq * 8)) = u;
@@ -329,7 +344,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint4 u = *reinterpret_cast<const uint4*>(sX + sw_off(t, hc * 32 + qq * 8));
                 xreg[qq * 4 + 0] = u.x; xreg[qq * 4 + 1] = u.y; xreg[qq * 4 + 2] = u.z; xreg[qq * 4 + 3] = u.w;
             }
-            scale_half_row<BF16>(sC, t, hc, EL[t]);
             scale_half_row<BF16>(sB, t, hc, Wj[t]);
             uint8_t* sS = sm + OFF_S;
             const float dch = __expf(lend);
@@ -353,20 +367,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_proxy_async_shared();
         tc::tc_fence_before();
         __syncthreads();
-        // -- Y(c) = M X + C' S_old into TMEM buffer c & 1 ; S += B~^T X ; then CB(c+1)
+        // -- Y(c) = M X and CS(c) = C S_old into TMEM buffers c & 1 ; S += B~^T X ; then CB(c+1)
         if (tid == 0) {
             tc::tc_fence_after();
             const uint32_t sMa = smem_u32(sm + OFF_M), sXa = smem_u32(sX), sSa = smem_u32(sm + OFF_S);
             const uint32_t sCa = smem_u32(sC), sBa = smem_u32(sB);
-            const uint32_t ty = tmem + T_Y + buf * 64;
+            const uint32_t ty = tmem + T_Y + buf * 64, tcs = tmem + T_CS + buf * 64;
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
                 tc::umma_f16(ty, tc::sw128_desc(sMa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
                              tc::sw128_desc(sXa + k * 2048, PANEL, 1024), ID_Y, k > 0);
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
-                tc::umma_f16(ty, tc::sw128_desc(sCa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
-                             tc::sw128_desc(sSa + k * 2048, PANEL, 1024), ID_Y, 1);
+                tc::umma_f16(tcs, tc::sw128_desc(sCa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
+                             tc::sw128_desc(sSa + k * 2048, PANEL, 1024), ID_Y, k > 0);
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k)
                 tc::umma_f16(tmem + T_S, tc::sw128_desc(sBa + k * 2048, PANEL, 1024),
@@ -378,9 +392,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         // -- while MMA 2 (c) runs: chunk c+1's dt scan, chunk c-1's epilogue
         if (warp == 0 && c + 1 < nc) scan_dt(c + 1);
-        if (c > 0) epilogue(c - 1, xprev);
+        if (c > 0) epilogue(c - 1, xprev, elprev);
 #pragma unroll
         for (int e = 0; e < 16; ++e) xprev[e] = xreg[e];
+        elprev = elcur;
         if (!tc::mbar_wait(bar_y, c & 1, abort_flag)) { ok = false; break; }
         tc::tc_fence_after();
         // this chunk's buffer is free now: prefetch chunk c + 2 into it
@@ -392,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok && !*abort_flag && nc > 0) {
         tc::tc_fence_after();
-        epilogue(nc - 1, xprev);
+        epilogue(nc - 1, xprev, elprev);
     }
 
     if (ok && !*abort_flag) {   // final state -> global
