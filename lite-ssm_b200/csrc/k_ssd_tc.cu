@@ -321,6 +321,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
             for (uint32_t jc = 0; jc < 2; ++jc) {
                 const uint32_t col0 = hc * 64 + jc * 32;
+                if (col0 > q4 * 32 + 31) {   // above the diagonal for every row of this warp: zeros
+#pragma unroll
+                    for (int qq = 0; qq < 4; ++qq)
+                        *reinterpret_cast<uint4*>(sM + sw_off(t, col0 + qq * 8)) = make_uint4(0, 0, 0, 0);
+                    continue;
+                }
                 uint32_t v[32];
                 tc::tmem_ld32(tmem + lane_base + T_CB + col0, v);
                 tc::tmem_ld_wait();
