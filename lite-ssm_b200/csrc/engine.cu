@@ -38,8 +38,6 @@ cudaError_t launch_conv_update_silu_split(const void* xbc, uint64_t in_stride, v
                                           uint32_t GN, uint32_t K, cudaStream_t s);
 cudaError_t launch_seed_strided(const void* xbc, uint64_t in_stride, void* state, uint32_t B, uint32_t L, uint32_t D,
                                 uint32_t K, cudaStream_t s);
-cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
-                        cudaStream_t s);
 cudaError_t launch_synth_f16(void* out, uint64_t n, uint64_t seed, uint64_t stream, float amp, cudaStream_t s);
 cudaError_t launch_synth_int4(void* out, uint32_t N, uint32_t K, uint64_t seed, uint64_t stream, float amp,
                               cudaStream_t s);
@@ -1030,14 +1028,14 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         SsdArgs a{};
         a.X = s->xs; a.B = s->Bs; a.C = s->Cs; a.dt_raw = dtc;
         a.dt_bias = lw.dt_bias; a.A_log = lw.A_log; a.D = lw.D;
-        a.Y = s->ys; a.state = ssd;
+        a.Y = s->gated; a.state = ssd;   // gated output: the gate is applied in the scan's epilogue
+        a.z = zc; a.z_row_stride = proj;
         a.batch = B; a.L = L; a.H = H; a.P = P; a.N = N; a.G = s->G; a.chunk = h.chunk_size;
         a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
         a.x_dtype = 0; a.dt_dtype = 0; a.param_dtype = 0; a.y_dtype = 0;
         a.x_row_stride = di; a.bc_row_stride = GN; a.dt_row_stride = proj; a.y_row_stride = di;
         CU(launch_ssd_chunked(a, st));
-        CU(launch_gate(zc, proj, s->ys, s->gated, rows, di, st));
-        s->nl += 3;
+        s->nl += 2;
     }
     // 7+8+9. gated RMSNorm + out_proj + residual add into hidden
     if (s->comm && decode && s->use_p2p && comm_p2p(s->comm, (size_t)rows * dm)) {

@@ -68,11 +68,86 @@ __global__ void k_conv_silu_split(const __half* __restrict__ xbc, uint64_t in_st
     }
 }
 
+// Vectorised form (d_conv == 4, 8 channels per thread, 16-byte loads and stores): the
+// same arithmetic per channel. Needs in_stride, d_inner and GN multiples of 8 and 16-byte
+// aligned rows, so an octet never straddles the x / B / C boundaries.
+constexpr uint32_t CT8 = 32;   // tokens per thread
+__global__ void __launch_bounds__(128) k_conv4_silu_split8(const __half* __restrict__ xbc, uint64_t in_stride,
+                                                           const __half* __restrict__ w,
+                                                           const __half* __restrict__ bias, __half* __restrict__ xo,
+                                                           __half* __restrict__ bo, __half* __restrict__ co, uint32_t L,
+                                                           uint32_t d_inner, uint32_t GN) {
+    const uint32_t D = d_inner + 2 * GN;
+    const uint32_t d0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    const uint32_t t0 = blockIdx.y * CT8, b = blockIdx.z;
+    if (d0 >= D) return;
+    const __half* xb = xbc + (uint64_t)b * L * in_stride + d0;
+    float wk[8][4], bv[8], win[3][8];
+    {
+        const uint4* w4 = reinterpret_cast<const uint4*>(w + (uint64_t)d0 * 4);   // 8 channels x 4 taps
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 u = w4[q];
+            const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) wk[q * 2 + e / 4][e % 4] = __half2float(h[e]);
+        }
+        const uint4 bu = *reinterpret_cast<const uint4*>(bias + d0);
+        const __half* bh = reinterpret_cast<const __half*>(&bu);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bv[e] = __half2float(bh[e]);
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int src = (int)t0 - 3 + k;
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (src >= 0) u = *reinterpret_cast<const uint4*>(xb + (uint64_t)src * in_stride);
+        const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) win[k][e] = __half2float(h[e]);
+    }
+    __half* dst;
+    uint32_t ds;
+    if (d0 < d_inner) { dst = xo + d0; ds = d_inner; }
+    else if (d0 < d_inner + GN) { dst = bo + (d0 - d_inner); ds = GN; }
+    else { dst = co + (d0 - d_inner - GN); ds = GN; }
+    const uint32_t tend = min(t0 + CT8, L);
+    for (uint32_t t = t0; t < tend; ++t) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xb + (uint64_t)t * in_stride);
+        const __half* h = reinterpret_cast<const __half*>(&u);
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float xn = __half2float(h[e]);
+            float acc = bv[e];
+            acc += wk[e][0] * win[0][e];
+            acc += wk[e][1] * win[1][e];
+            acc += wk[e][2] * win[2][e];
+            acc += wk[e][3] * xn;
+            oh[e] = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
+            win[0][e] = win[1][e];
+            win[1][e] = win[2][e];
+            win[2][e] = xn;
+        }
+        *reinterpret_cast<uint4*>(dst + ((uint64_t)b * L + t) * ds) = o;
+    }
+}
+
 cudaError_t launch_conv_silu_split(const void* xbc, uint64_t in_stride, const void* w, const void* bias, void* xo,
                                    void* bo, void* co, uint32_t B, uint32_t L, uint32_t d_inner, uint32_t GN,
                                    uint32_t K, cudaStream_t s) {
     const uint32_t D = d_inner + 2 * GN;
     if (!B || !L || K == 0 || K > 8) return K > 8 ? cudaErrorInvalidValue : cudaSuccess;
+    if (K == 4 && in_stride % 8 == 0 && d_inner % 8 == 0 && GN % 8 == 0 && aligned(xbc, 16) && aligned(w, 16) &&
+        aligned(bias, 16) && aligned(xo, 16) && aligned(bo, 16) && aligned(co, 16)) {
+        dim3 grid((D / 8 + 127) / 128, (L + CT8 - 1) / CT8, B);
+        k_conv4_silu_split8<<<grid, 128, 0, s>>>(static_cast<const __half*>(xbc), in_stride,
+                                                 static_cast<const __half*>(w), static_cast<const __half*>(bias),
+                                                 static_cast<__half*>(xo), static_cast<__half*>(bo),
+                                                 static_cast<__half*>(co), L, d_inner, GN);
+        return cudaGetLastError();
+    }
     dim3 grid((D + 127) / 128, (L + CT - 1) / CT, B);
     k_conv_silu_split<<<grid, 128, 0, s>>>(static_cast<const __half*>(xbc), in_stride, static_cast<const __half*>(w),
                                            static_cast<const __half*>(bias), static_cast<__half*>(xo),
@@ -140,8 +215,8 @@ cudaError_t launch_seed_strided(const void* xbc, uint64_t in_stride, void* state
 }
 
 // gated[r, c] = half(silu(z[r*z_stride + c]) * y[r*d + c])
-__global__ void k_gate(const __half* __restrict__ z, uint64_t z_stride, const __half* __restrict__ y,
-                       __half* __restrict__ out, uint32_t rows, uint32_t d) {
+__global__ void k_gate(const __half* __restrict__ z, uint64_t z_stride, const __half* y, __half* out, uint32_t rows,
+                       uint32_t d) {
     const uint64_t total = (uint64_t)rows * d;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t r = i / d, c = i % d;
@@ -149,10 +224,36 @@ __global__ void k_gate(const __half* __restrict__ z, uint64_t z_stride, const __
     }
 }
 
+// 8 elements per thread with 16-byte accesses (d, z_stride multiples of 8, aligned rows).
+__global__ void k_gate8(const __half* __restrict__ z, uint64_t z_stride, const __half* y, __half* out, uint32_t rows,
+                        uint32_t d) {
+    const uint32_t d8 = d / 8;
+    const uint64_t total = (uint64_t)rows * d8;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / d8, c = (i % d8) * 8;
+        const uint4 zu = *reinterpret_cast<const uint4*>(z + r * z_stride + c);
+        const uint4 yu = *reinterpret_cast<const uint4*>(y + r * d + c);
+        const __half* zh = reinterpret_cast<const __half*>(&zu);
+        const __half* yh = reinterpret_cast<const __half*>(&yu);
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) oh[e] = __float2half_rn(silu(__half2float(zh[e])) * __half2float(yh[e]));
+        *reinterpret_cast<uint4*>(out + r * d + c) = o;
+    }
+}
+
 cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
                         cudaStream_t s) {
     const uint64_t n = (uint64_t)rows * d;
     if (!n) return cudaSuccess;
+    if (d % 8 == 0 && z_stride % 8 == 0 && aligned(z, 16) && aligned(y, 16) && aligned(out, 16)) {
+        uint64_t g = (n / 8 + 255) / 256;
+        if (g > 148 * 16) g = 148 * 16;
+        k_gate8<<<(unsigned)g, 256, 0, s>>>(static_cast<const __half*>(z), z_stride, static_cast<const __half*>(y),
+                                            static_cast<__half*>(out), rows, d);
+        return cudaGetLastError();
+    }
     uint64_t g = (n + 255) / 256;
     if (g > 148 * 32) g = 148 * 32;
     k_gate<<<(unsigned)g, 256, 0, s>>>(static_cast<const __half*>(z), z_stride, static_cast<const __half*>(y),

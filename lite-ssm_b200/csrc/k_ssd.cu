@@ -300,7 +300,12 @@ cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     k_ssd_chunked_simt<<<a.batch * a.H, SSD_THREADS, smem, s>>>(a);
-    return cudaGetLastError();
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !a.z) return e;
+    // the general-shape kernel writes y; gate it in place
+    const uint64_t yrs = a.y_row_stride ? a.y_row_stride : (uint64_t)a.H * a.P;
+    if (yrs != (uint64_t)a.H * a.P || a.y_dtype != 0) return cudaErrorInvalidValue;
+    return launch_gate(a.z, a.z_row_stride, a.Y, a.Y, a.batch * a.L, a.H * a.P, s);
 }
 
 }  // namespace lssm

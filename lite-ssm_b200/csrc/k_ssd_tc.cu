@@ -54,6 +54,7 @@ constexpr uint32_t T_CB = 0, T_Y = 128, T_CS = 256, T_S = 384, TMEM_COLS = 512;
 struct TcArgs {
     const void* dt_raw; const void* dt_bias; const void* A_log; const void* D;
     void* Y; float* state;
+    const __half* z; uint64_t z_rs;   // optional gate: Y = half(silu(z) * half(y))
     uint32_t batch, L, H, P, N, G;
     float dt_min, dt_max;
     uint32_t has_D;
@@ -276,6 +277,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int qq = 0; qq < 8; ++qq)
                     dst[qq] = make_float4(y[4 * qq], y[4 * qq + 1], y[4 * qq + 2], y[4 * qq + 3]);
+            } else if (a.z) {   // gated: half(silu(z) * half(y)), fp16
+                const uint4* zs = reinterpret_cast<const uint4*>(
+                    a.z + ((uint64_t)b * a.L + t0 + t) * a.z_rs + (uint64_t)h * TP + hc * 32);
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                    const uint4 zu = zs[qq];
+                    const __half* zh = reinterpret_cast<const __half*>(&zu);
+                    uint4 u;
+                    __half* oh = reinterpret_cast<__half*>(&u);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float yv = __half2float(__float2half_rn(y[qq * 8 + e]));
+                        oh[e] = __float2half_rn(silu(__half2float(zh[e])) * yv);
+                    }
+                    dst[qq] = u;
+                }
             } else {
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
 #pragma unroll
@@ -468,6 +486,7 @@ cudaError_t launch_ssd_chunked_tc(const SsdArgs& s, cudaStream_t st) {
     if (xrs % 8 || bcrs % 8 || yrs % 8 || s.batch == 0 || s.L == 0) return cudaErrorNotSupported;
     if (!aligned(s.X, 16) || !aligned(s.B, 16) || !aligned(s.C, 16) || !aligned(s.Y, 16))
         return cudaErrorNotSupported;
+    if (s.z && (s.y_dtype != 0 || s.z_row_stride % 8 || !aligned(s.z, 16))) return cudaErrorNotSupported;
     const bool bf16 = s.x_dtype == 1;
     CUtensorMap mx, mb, mc;
     if (!make_map3(&mx, s.X, xrs, s.L, s.batch, xrs, bf16) || !make_map3(&mb, s.B, bcrs, s.L, s.batch, bcrs, bf16) ||
@@ -475,6 +494,7 @@ cudaError_t launch_ssd_chunked_tc(const SsdArgs& s, cudaStream_t st) {
         return cudaErrorNotSupported;
     TcArgs a{};
     a.dt_raw = s.dt_raw; a.dt_bias = s.dt_bias; a.A_log = s.A_log; a.D = s.D; a.Y = s.Y; a.state = s.state;
+    a.z = static_cast<const __half*>(s.z); a.z_rs = s.z_row_stride;
     a.batch = s.batch; a.L = s.L; a.H = s.H; a.P = s.P; a.N = s.N; a.G = s.G ? s.G : 1;
     a.dt_min = s.dt_min; a.dt_max = s.dt_max; a.has_D = s.has_D;
     a.dt_dtype = s.dt_dtype; a.param_dtype = s.param_dtype; a.y_dtype = s.y_dtype;

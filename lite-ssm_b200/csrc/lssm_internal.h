@@ -101,8 +101,15 @@ struct SsdArgs {
     uint32_t x_dtype, dt_dtype, param_dtype, y_dtype;
     // Element strides (in elements) for X/Y rows, B/C rows and dt rows; 0 = dense default.
     uint64_t x_row_stride, bc_row_stride, dt_row_stride, y_row_stride;
+    // Optional gate (model prefill): when z is set (fp16, rows of z_row_stride, y_dtype f16),
+    // Y receives the gated half(silu(z) * half(y)) instead of y (mamba2_block.cpp:231-234).
+    const void* z = nullptr;
+    uint64_t z_row_stride = 0;
 };
 cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s);
+// out[r][c] = half(silu(z[r * z_stride + c]) * y[r][c]) over rows x d (y and out dense; may alias).
+cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
+                        cudaStream_t s);
 
 // ssd_step over `batch` sequences with per-sequence strides (elements). When z is set
 // the output is the gated value half(silu(z) * half(y)) instead of y.

@@ -92,8 +92,10 @@ def test_synthesized_model_bit_exact_vs_cpu(ctx, int4):
     assert gpu == cpu
 
 
-def test_synthesized_model_generation_vs_oracle(ctx):
-    hp = dict(d_model=256, n_layer=3, d_state=64, d_conv=4, expand=2, vocab_size=512, n_heads=8, d_head=64,
+@pytest.mark.parametrize("d_state", [64, 128])
+def test_synthesized_model_generation_vs_oracle(ctx, d_state):
+    """d_state 128 with d_head 64 takes the tensor-core scan (gate fused into its epilogue)."""
+    hp = dict(d_model=256, n_layer=3, d_state=d_state, d_conv=4, expand=2, vocab_size=512, n_heads=8, d_head=64,
               chunk_size=64, n_groups=1, norm_before_gate=0)
     m = lssm.Model.synthesize(ctx, lssm.hparams(**hp), seed=5, int4=True)
     prompt = np.random.default_rng(9).integers(0, 512, size=(1, 130)).astype(np.uint32)
@@ -102,6 +104,7 @@ def test_synthesized_model_generation_vs_oracle(ctx):
     ora = po.OracleModel(m.download_bytes(), mode=0)
     otoks, opre, ostep = ora.generate(prompt[0], 8, teacher=toks)
     assert near_tie_ok(toks, otoks, np.concatenate([opre[None], ostep]))
+    assert np.abs(s.logits()[0] - ostep[-1]).max() < 0.1
 
 
 def test_synthesized_batch4_vs_oracle(ctx):
