@@ -1,7 +1,7 @@
 // k_ssd_tc.cu — SSD chunked scan on the 5th-generation tensor cores
 // (shaders/ssd_chunked.metal:82-297 restated for P = 64, N = 128).
 //
-// One CTA (256 threads: two warps per TMEM lane quarter, splitting the columns) per
+// One CTA (512 threads: four warps per TMEM lane quarter, splitting the columns) per
 // (sequence b, head h) walks the sequence in chunks of
 // Q = 128 tokens. The fp32 state S (N x P) lives in TMEM for the whole walk. Per chunk:
 //   inputs   X_c (Q x P), B_c, C_c (Q x N) arrive by TMA (128-byte swizzled,
@@ -34,7 +34,7 @@ namespace lssm {
 namespace {
 
 constexpr int TQ = 128, TP = 64, TN = 128;
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;   // 4 warps per TMEM lane quarter, each a quarter of the columns
 // shared-memory map (offsets from a 1024-byte aligned base)
 constexpr uint32_t X_BYTES = TQ * TP * 2;          // 16 KB
 constexpr uint32_t BC_BYTES = TQ * TN * 2;         // 32 KB (two 64-column panels of 16 KB)
@@ -94,34 +94,13 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
     return __half22float2(*reinterpret_cast<__half2*>(&u));
 }
 
-// Scale one 128-element row (2 panels) of a swizzled 16-bit tile in place. Thread
-// `row` visits its 16-byte chunks in an order rotated by (row & 7), so the 32 threads
-// of a warp hit 8 different bank groups at every step (no 32-way conflicts).
+// Scale the 32-element quarter `hq` (half a panel) of a row of a swizzled tile in place.
 template <bool BF16>
-__device__ __forceinline__ void scale_row(uint8_t* tile, uint32_t row, float s) {
+__device__ __forceinline__ void scale_quarter_row(uint8_t* tile, uint32_t row, uint32_t hq, float s) {
 #pragma unroll
-    for (int ch = 0; ch < 16; ++ch) {
-        const uint32_t c8 = ((uint32_t)ch & 7) ^ (row & 7);
-        uint4* p = reinterpret_cast<uint4*>(tile + (ch >> 3) * PANEL + row * 128 + c8 * 16);
-        uint4 u = *p;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float2 f = unpack2<BF16>(w[i]);
-            w[i] = pack2<BF16>(f.x * s, f.y * s);
-        }
-        *p = u;
-    }
-}
-
-
-// Scale the 64-element half `hc` (one panel) of a row of a swizzled tile in place.
-template <bool BF16>
-__device__ __forceinline__ void scale_half_row(uint8_t* tile, uint32_t row, uint32_t hc, float s) {
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t c8 = ((uint32_t)ch) ^ (row & 7);
-        uint4* p = reinterpret_cast<uint4*>(tile + hc * PANEL + row * 128 + c8 * 16);
+    for (int ch = 0; ch < 4; ++ch) {
+        const uint32_t c8 = ((hq & 1) * 4 + (uint32_t)ch) ^ (row & 7);
+        uint4* p = reinterpret_cast<uint4*>(tile + (hq >> 1) * PANEL + row * 128 + c8 * 16);
         uint4 u = *p;
         uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
@@ -207,10 +186,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     // initial state S[p][n] -> TMEM lane n, columns T_S + p (this thread: p in [hc*32, hc*32+32))
     {
-        uint32_t v[32];
+        uint32_t v[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(Sg[(uint64_t)(hc * 32 + j) * TN + t]);
-        tc::tmem_st32(tmem + lane_base + T_S + hc * 32, v);
+        for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(Sg[(uint64_t)(hc * 16 + j) * TN + t]);
+        tc::tmem_st16(tmem + lane_base + T_S + hc * 16, v);
         tc::tmem_st_wait();
     }
     // dt of chunk 0 (warp 0, 4 tokens per lane), software-pipelined one chunk ahead
@@ -255,34 +234,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             F[3 * TQ + tt] = __expf(pre);
         }
     };
-    // y_t = Y_t + exp(Lc_t) CS_t + D x_t for chunk c (columns hc*32 .. +32), Y and CS from
+    // y_t = Y_t + exp(Lc_t) CS_t + D x_t for chunk c (columns hc*16 .. +16), Y and CS from
     // TMEM buffers c & 1; el = exp(Lc_t) of this thread's row
-    auto epilogue = [&](uint32_t c, const uint32_t (&xr)[16], float el) {
+    auto epilogue = [&](uint32_t c, const uint32_t (&xr)[8], float el) {
         const uint32_t t0 = c * TQ, tl = min((uint32_t)TQ, a.L - t0);
-        uint32_t v[32], w[32];
-        tc::tmem_ld32(tmem + lane_base + T_Y + (c & 1) * 64 + hc * 32, v);
-        tc::tmem_ld32(tmem + lane_base + T_CS + (c & 1) * 64 + hc * 32, w);
+        uint32_t v[16], w[16];
+        tc::tmem_ld16(tmem + lane_base + T_Y + (c & 1) * 64 + hc * 16, v);
+        tc::tmem_ld16(tmem + lane_base + T_CS + (c & 1) * 64 + hc * 16, w);
         tc::tmem_ld_wait();
         if (t < tl) {
-            float y[32];
+            float y[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8; ++e) {
                 const float2 xv = unpack2<BF16>(xr[e]);
                 y[2 * e] = __uint_as_float(v[2 * e]) + el * __uint_as_float(w[2 * e]) + Dh * xv.x;
                 y[2 * e + 1] = __uint_as_float(v[2 * e + 1]) + el * __uint_as_float(w[2 * e + 1]) + Dh * xv.y;
             }
-            const uint64_t o = ((uint64_t)b * a.L + t0 + t) * a.y_rs + (uint64_t)h * TP + hc * 32;
+            const uint64_t o = ((uint64_t)b * a.L + t0 + t) * a.y_rs + (uint64_t)h * TP + hc * 16;
             if (a.y_dtype == 2) {
                 float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.Y) + o);
 #pragma unroll
-                for (int qq = 0; qq < 8; ++qq)
+                for (int qq = 0; qq < 4; ++qq)
                     dst[qq] = make_float4(y[4 * qq], y[4 * qq + 1], y[4 * qq + 2], y[4 * qq + 3]);
             } else if (a.z) {   // gated: half(silu(z) * half(y)), fp16
                 const uint4* zs = reinterpret_cast<const uint4*>(
-                    a.z + ((uint64_t)b * a.L + t0 + t) * a.z_rs + (uint64_t)h * TP + hc * 32);
+                    a.z + ((uint64_t)b * a.L + t0 + t) * a.z_rs + (uint64_t)h * TP + hc * 16);
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
 #pragma unroll
-                for (int qq = 0; qq < 4; ++qq) {
+                for (int qq = 0; qq < 2; ++qq) {
                     const uint4 zu = zs[qq];
                     const __half* zh = reinterpret_cast<const __half*>(&zu);
                     uint4 u;
@@ -297,7 +276,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             } else {
                 uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.Y) + o);
 #pragma unroll
-                for (int qq = 0; qq < 4; ++qq) {
+                for (int qq = 0; qq < 2; ++qq) {
                     uint4 u;
                     uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
@@ -310,10 +289,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     };
     if (warp == 0) scan_dt(0);
-    uint32_t xprev[16];   // x rows of the chunk whose epilogue is pending
+    uint32_t xprev[8];    // x rows of the chunk whose epilogue is pending
     float elprev = 0.0f;  // and its exp(Lc_t)
 #pragma unroll
-    for (int e = 0; e < 16; ++e) xprev[e] = 0;
+    for (int e = 0; e < 8; ++e) xprev[e] = 0;
 
     for (uint32_t c = 0; c < nc && ok; ++c) {
         const uint32_t buf = c & 1;
@@ -331,14 +310,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!tc::mbar_wait(bar_cb, c & 1, abort_flag)) { ok = false; break; }
         tc::tc_fence_after();
         const float lend = Lc[TQ - 1];
-        uint32_t xreg[16];   // x_t[hc*32 .. +32] packed, kept for the epilogue
+        uint32_t xreg[8];    // x_t[hc*16 .. +16] packed, kept for the epilogue
         const float elcur = EL[t];
         {
             const float lct2 = Lc[t] * LOG2E;
             uint8_t* sM = sm + OFF_M;
 #pragma unroll 1
-            for (uint32_t jc = 0; jc < 2; ++jc) {
-                const uint32_t col0 = hc * 64 + jc * 32;
+            for (uint32_t jc = 0; jc < 1; ++jc) {
+                const uint32_t col0 = hc * 32;
                 if (col0 > q4 * 32 + 31) {   // above the diagonal for every row of this warp: zeros
 #pragma unroll
                     for (int qq = 0; qq < 4; ++qq)
@@ -364,28 +343,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-                const uint4 u = *reinterpret_cast<const uint4*>(sX + sw_off(t, hc * 32 + qq * 8));
+            for (int qq = 0; qq < 2; ++qq) {
+                const uint4 u = *reinterpret_cast<const uint4*>(sX + sw_off(t, hc * 16 + qq * 8));
                 xreg[qq * 4 + 0] = u.x; xreg[qq * 4 + 1] = u.y; xreg[qq * 4 + 2] = u.z; xreg[qq * 4 + 3] = u.w;
             }
-            scale_half_row<BF16>(sB, t, hc, Wj[t]);
+            scale_quarter_row<BF16>(sB, t, hc, Wj[t]);
             uint8_t* sS = sm + OFF_S;
             const float dch = __expf(lend);
-            uint32_t v[32];
-            tc::tmem_ld32(tmem + lane_base + T_S + hc * 32, v);
+            uint32_t v[16];
+            tc::tmem_ld16(tmem + lane_base + T_S + hc * 16, v);
             tc::tmem_ld_wait();
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
+            for (int qq = 0; qq < 2; ++qq) {
                 uint4 u;
                 uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
                     w[e] = pack2<BF16>(__uint_as_float(v[qq * 8 + e * 2]), __uint_as_float(v[qq * 8 + e * 2 + 1]));
-                *reinterpret_cast<uint4*>(sS + sw_off(t, hc * 32 + qq * 8)) = u;
+                *reinterpret_cast<uint4*>(sS + sw_off(t, hc * 16 + qq * 8)) = u;
             }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * dch);
-            tc::tmem_st32(tmem + lane_base + T_S + hc * 32, v);
+            for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * dch);
+            tc::tmem_st16(tmem + lane_base + T_S + hc * 16, v);
             tc::tmem_st_wait();
         }
         tc::fence_proxy_async_shared();
@@ -418,7 +397,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (warp == 0 && c + 1 < nc) scan_dt(c + 1);
         if (c > 0) epilogue(c - 1, xprev, elprev);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) xprev[e] = xreg[e];
+        for (int e = 0; e < 8; ++e) xprev[e] = xreg[e];
         elprev = elcur;
         if (!tc::mbar_wait(bar_y, c & 1, abort_flag)) { ok = false; break; }
         tc::tc_fence_after();
@@ -436,11 +415,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (ok && !*abort_flag) {   // final state -> global
         tc::tc_fence_after();
-        uint32_t v[32];
-        tc::tmem_ld32(tmem + lane_base + T_S + hc * 32, v);
+        uint32_t v[16];
+        tc::tmem_ld16(tmem + lane_base + T_S + hc * 16, v);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) Sg[(uint64_t)(hc * 32 + j) * TN + t] = __uint_as_float(v[j]);
+        for (int j = 0; j < 16; ++j) Sg[(uint64_t)(hc * 16 + j) * TN + t] = __uint_as_float(v[j]);
     }
     // teardown: pending TMA and tensor-core work must finish before exit (bounded)
     if (tid == 0 && *abort_flag) {
