@@ -1,4 +1,4 @@
-"""Benchmark of the B200 Mamba-2 hot path (the BASELINE metric: 2.7B-shape INT4
+"""Benchmark of the B200 Mamba-2 hot path (the headline metric: 2.7B-shape INT4
 decode / prefill tokens per second, with roofline fractions).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -409,7 +409,7 @@ def run_ours(args, world, rank, local, dist):
 
 
 def run_kernel_bench(args):
-    """Single-kernel microbenchmarks at the BASELINE shapes (used for the roofline
+    """Single-kernel microbenchmarks at the benchmark shapes (used for the roofline
     numbers and as small, bounded cases for ncu). Weights / states are cycled over
     64 distinct layer slices so every launch reads from HBM (> 126 MB L2), like a
     real decode token does."""
@@ -550,7 +550,7 @@ def run_kernel_bench(args):
 
 
 def run_batched(args, world, rank, local, dist):
-    """Batched decode (the BASELINE batched config): `--seqs` independent sequences (default
+    """Batched decode (the batched benchmark config): `--seqs` independent sequences (default
     64), each a 512-token prompt + 256 greedy decode steps, sharded over the ranks (seqs /
     world per GPU, weights replicated, no data-path collective): strong scaling."""
     import lssm

@@ -11,7 +11,7 @@
 //
 // Peer exchange (comm_p2p_setup, collective): every rank allocates a receive area
 // [2 parities][world][cap] of 8-byte words (value + epoch) and maps every peer's area
-// through CUDA IPC (plain peer stores over NVLink; no multicast object). It is enabled only
+// through CUDA IPC (plain peer stores over NVLink, point to point). It is enabled only
 // when all ranks sit on distinct GPUs with peer access: the exchange kernels poll for words
 // that other ranks' kernels write, which must never share one GPU.
 #include <dlfcn.h>
