@@ -688,15 +688,17 @@ int* tc_error_word();
 //  Each CTA stages its (optionally RMS-normalised) input rows once, in the fragment
 //  order of k_gemv_int4_tma, then streams its 16-row tiles (tile = blockIdx.x + i *
 //  gridDim.x) through a ring of `nst` shared-memory stages. A stage is one K chunk
-//  (KC = 256 * segl k) of one tile, brought by two tensor-map copies issued by warp 7:
-//  the packed rows viewed as [K/256 lines][N rows][128 B] (box segl x 16 x 128 B,
-//  128-byte swizzle, so smem line = s * 16 + r and the 8 rows an MMA fragment reads
-//  fall in 8 different swizzle phases: conflict-free) and the scales viewed the same
-//  way as [K/256 lines][N rows][8 scales] (box segl x 16 x 16 B: a row's scales of one
-//  line are 16 B from the next row's, so the 8 rows' scale reads hit 8 bank groups). Warps 0..6 split the chunk's 32-k blocks, run the exact dequant +
-//  m16n8k16 MMA of k_gemv_int4_tma, release the stage (empty barrier, 7 arrivals) and
-//  at the end of a tile reduce their partials through a double-buffered shared array
-//  (one named barrier per tile). Up to nst stages are in flight per SM.
+//  (KC = 256 * segl k) of one 32-row tile, brought by two tensor-map copies issued by
+//  warp 15: the packed rows viewed as [K/256 lines][N rows][128 B] (box segl x 32 x
+//  128 B, 128-byte swizzle, so smem line = s * 32 + r and the 8 rows an MMA fragment
+//  reads fall in 8 different swizzle phases: conflict-free) and the scales viewed the
+//  same way as [K/256 lines][N rows][8 scales] (box segl x 32 x 16 B: a row's scales of
+//  one line are 16 B from the next row's, so the 8 rows' scale reads hit 8 bank groups).
+//  Warps 0..14 split the stage's (16-row sub-tile, 32-k block) items, run the
+//  bias-folded dequant (dequant_word_fold) + m16n8k16 MMAs, release the stage (empty
+//  barrier, 15 arrivals) and at the end of a tile reduce their partials through a
+//  double-buffered shared array (one named barrier per tile). Up to nst stages are in
+//  flight per SM.
 //  Every wait is bounded (2 s); a timeout raises *err, the consumers stop computing but
 //  keep the tile barriers, and the producer waits (bounded) for its own copies before
 //  the CTA exits.
@@ -716,6 +718,8 @@ __device__ __forceinline__ void st_mbar_expect(uint32_t bar, uint32_t bytes) {
                  : "memory");
 }
 
+constexpr uint32_t ST_ROWS = 32;   // rows per tile (two 16-row MMA sub-tiles)
+
 template <int EPI>
 __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_constant__ CUtensorMap wmap,
                                                             const __grid_constant__ CUtensorMap smap,
@@ -726,7 +730,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
                                                             int* __restrict__ err) {
     extern __shared__ __align__(128) uint8_t smem_st[];
     __shared__ __align__(8) uint64_t full[ST_MAX], empty[ST_MAX];
-    __shared__ float part[2][ST_CONS][32][4];
+    __shared__ float part[2][2][ST_CONS][32][4];   // [tile parity][sub-tile][warp][lane][fragment]
     __shared__ float red[32];
     __shared__ float rr[GEMV_MMAX];
     __shared__ volatile int abort_flag;
@@ -735,8 +739,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
     uint4* xs = reinterpret_cast<uint4*>(ring + (size_t)nst * stage_bytes);
     float* corr = reinterpret_cast<float*>(xs + (size_t)M * (K / 8));   // [K/32][8]
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t ntiles = (N + 15) / 16, KC = 256 * segl, nchunk = K / KC;
-    const uint32_t wbytes = segl * 16 * 128, sc_bytes = KC / 32 * 2;
+    const uint32_t ntiles = (N + ST_ROWS - 1) / ST_ROWS, KC = 256 * segl, nchunk = K / KC;
+    const uint32_t wbytes = segl * ST_ROWS * 128, sbytes = segl * ST_ROWS * 16;
     const uint32_t my_tiles = blockIdx.x < ntiles ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
     const uint32_t total = my_tiles * nchunk;
     if (threadIdx.x == 0) {
@@ -748,14 +752,14 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    auto issue = [&](uint32_t q, uint64_t pol) {   // lane 0 of warp 7: stage q = (tile, chunk)
+    auto issue = [&](uint32_t q, uint64_t pol) {   // lane 0 of the producer warp: stage q = (tile, chunk)
         const uint32_t slot = q % nst;
         const uint32_t t = blockIdx.x + (q / nchunk) * gridDim.x, ch = q % nchunk;
         const uint32_t fb = smem_u32(&full[slot]);
         const uint32_t st = smem_u32(ring + (size_t)slot * stage_bytes);
-        st_mbar_expect(fb, wbytes + 16 * sc_bytes);
-        tma3(st, &wmap, 0, (int32_t)(t * 16), (int32_t)(ch * segl), fb, pol);
-        tma3(st + wbytes, &smap, 0, (int32_t)(t * 16), (int32_t)(ch * segl), fb, pol);
+        st_mbar_expect(fb, wbytes + sbytes);
+        tma3(st, &wmap, 0, (int32_t)(t * ST_ROWS), (int32_t)(ch * segl), fb, pol);
+        tma3(st + wbytes, &smap, 0, (int32_t)(t * ST_ROWS), (int32_t)(ch * segl), fb, pol);
     };
     uint32_t issued = 0;
     uint64_t pol = 0;
@@ -787,15 +791,15 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
     }
 
     const uint32_t g = lane >> 2, c = lane & 3;
-    const uint32_t nbc = KC / 32;
+    const uint32_t nbc = KC / 32, items = 2 * nbc;   // (sub-tile, block) pairs per stage
     const bool has_x = g < M;
     const uint4* xrow = xs + (uint64_t)(has_x ? g : 0) * (K / 8) + c;
     const float2* corr2 = reinterpret_cast<const float2*>(corr) + c;   // rows (2c, 2c + 1) of block b at [4b]
     uint32_t q = 0;
     for (uint32_t i = 0; i < my_tiles; ++i) {
         const uint32_t t = blockIdx.x + i * gridDim.x;
-        const uint32_t row0 = t * 16;
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t row0 = t * ST_ROWS;
+        float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         for (uint32_t ch = 0; ch < nchunk; ++ch, ++q) {
             const uint32_t slot = q % nst;
             bool live = !abort_flag;
@@ -808,22 +812,22 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
             }
             if (live) {
                 const uint8_t* st = ring + (size_t)slot * stage_bytes;
-                // block b: line s = b / 8, 16-byte chunk j = b % 8, swizzled by the row's phase g & 7
-                const uint8_t* wa_base = st + g * 128 + 4 * c;
-                const uint8_t* wb_base = wa_base + 8 * 128;
-                // scale of (row r, block b): [b / 8][r][b % 8]
-                const __half* sa = reinterpret_cast<const __half*>(st + wbytes + g * 16);
-                const __half* sb = sa + 8 * 8;
+                // (sub-tile s, block b): rows s*16 + g (and + 8) on smem line (b / 8) * 32 + row,
+                // 16-byte chunk (b % 8) ^ g; scales at [b / 8][row][b % 8]
+                const uint8_t* w_base = st + g * 128 + 4 * c;
+                const __half* s_base = reinterpret_cast<const __half*>(st + wbytes) + g * 8;
                 const uint32_t gb0 = ch * nbc;
                 const uint4* xc = xrow + (uint64_t)gb0 * 4;
                 const float2* cc = corr2 + (uint64_t)gb0 * 4;
-                // blocks of the tile go round-robin over the consumer warps (balanced per tile)
-                const uint32_t bfirst = (warp + ST_CONS - gb0 % ST_CONS) % ST_CONS;
+                // (sub-tile, block) items go round-robin over the consumer warps (balanced per tile)
+                const uint32_t ifirst = (warp + ST_CONS - (ch * items) % ST_CONS) % ST_CONS;
 #pragma unroll 4
-                for (uint32_t b = bfirst; b < nbc; b += ST_CONS) {
-                    const uint32_t off = (b >> 3) * 2048 + (((b & 7) ^ g) << 4);
-                    const uint32_t wa = *reinterpret_cast<const uint32_t*>(wa_base + off);
-                    const uint32_t wb = *reinterpret_cast<const uint32_t*>(wb_base + off);
+                for (uint32_t it = ifirst; it < items; it += ST_CONS) {
+                    const uint32_t sub = it >= nbc, b = it - sub * nbc;
+                    const uint32_t line = (b >> 3) * 32 + sub * 16;
+                    const uint32_t off = line * 128 + (((b & 7) ^ g) << 4);
+                    const uint32_t wa = *reinterpret_cast<const uint32_t*>(w_base + off);
+                    const uint32_t wb = *reinterpret_cast<const uint32_t*>(w_base + off + 8 * 128);
                     const uint4 xf = has_x ? xc[b * 4] : make_uint4(0, 0, 0, 0);
                     const float2 cr = cc[b * 4];
                     uint32_t qa[4], qb[4];
@@ -834,12 +838,19 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
                     const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
                     mma_16816(d, a1, xf.x, xf.y);
                     mma_16816(d, a2, xf.z, xf.w);
-                    const uint32_t so = (b >> 3) * 128 + (b & 7);
-                    const float fa = __half2float(sa[so]), fb = __half2float(sb[so]);
-                    acc[0] += d[0] * fa;
-                    acc[1] += d[1] * fa;
-                    acc[2] += d[2] * fb;
-                    acc[3] += d[3] * fb;
+                    const uint32_t so = line * 8 + (b & 7);
+                    const float fa = __half2float(s_base[so]), fb = __half2float(s_base[so + 64]);
+                    if (sub) {
+                        acc1[0] += d[0] * fa;
+                        acc1[1] += d[1] * fa;
+                        acc1[2] += d[2] * fb;
+                        acc1[3] += d[3] * fb;
+                    } else {
+                        acc0[0] += d[0] * fa;
+                        acc0[1] += d[1] * fa;
+                        acc0[2] += d[2] * fb;
+                        acc0[3] += d[3] * fb;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) st_mbar_arrive(smem_u32(&empty[slot]));
@@ -847,14 +858,17 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
         }
         const uint32_t pb = i & 1;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) part[pb][warp][lane][j] = acc[j];
+        for (int j = 0; j < 4; ++j) {
+            part[pb][0][warp][lane][j] = acc0[j];
+            part[pb][1][warp][lane][j] = acc1[j];
+        }
         asm volatile("bar.sync 1, %0;" ::"n"(ST_CONS * 32) : "memory");
-        if (threadIdx.x < 128 && !abort_flag) {
-            const uint32_t l = threadIdx.x >> 2, j = threadIdx.x & 3;
+        if (threadIdx.x < 256 && !abort_flag) {
+            const uint32_t sub = threadIdx.x >> 7, l = (threadIdx.x & 127) >> 2, j = threadIdx.x & 3;
             float tsum = 0.0f;
 #pragma unroll
-            for (int w2 = 0; w2 < ST_CONS; ++w2) tsum += part[pb][w2][l][j];
-            const uint32_t row = row0 + (l >> 2) + ((j & 2) ? 8 : 0);
+            for (int w2 = 0; w2 < ST_CONS; ++w2) tsum += part[pb][sub][w2][l][j];
+            const uint32_t row = row0 + sub * 16 + (l >> 2) + ((j & 2) ? 8 : 0);
             const uint32_t m = (l & 3) * 2 + (j & 1);
             if (row < N && m < M) gemv_store<EPI>(y, (uint64_t)m * N + row, tsum);
         }
@@ -862,15 +876,15 @@ __global__ void __launch_bounds__(512, 1) k_gemv_int4_stream(const __grid_consta
 }
 
 // Tensor maps of one INT4_B32 matrix for k_gemv_int4_stream: packed rows as
-// [K/256 lines][N rows][128 B] (box segl x 16 x 128, 128-byte swizzle) and scales as
-// [K/256 lines][N rows][8 fp16] (box segl x 16 x 8).
+// [K/256 lines][N rows][128 B] (box segl x 32 x 128, 128-byte swizzle) and scales as
+// [K/256 lines][N rows][8 fp16] (box segl x 32 x 8).
 static bool stream_maps(CUtensorMap* wm, CUtensorMap* sm, const void* packed, const void* scales, uint32_t N,
                         uint32_t K, uint32_t segl) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t wd[3] = {128, N, K / 256};
     cuuint64_t ws[2] = {K / 2, 128};
-    cuuint32_t wbox[3] = {128, 16, segl};
+    cuuint32_t wbox[3] = {128, ST_ROWS, segl};
     cuuint32_t one[3] = {1, 1, 1};
     if (enc(wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(packed), wd, ws, wbox, one,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -878,7 +892,7 @@ static bool stream_maps(CUtensorMap* wm, CUtensorMap* sm, const void* packed, co
         return false;
     cuuint64_t sd[3] = {8, N, K / 256};
     cuuint64_t ss[2] = {K / 32 * 2, 16};
-    cuuint32_t sbox[3] = {8, 16, segl};
+    cuuint32_t sbox[3] = {8, ST_ROWS, segl};
     return enc(sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(scales), sd, ss, sbox, one,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -890,10 +904,9 @@ static cudaError_t launch_int4_stream(const void* x, const void* packed, const v
     const uint32_t lines = K / 256;
     uint32_t segl = 8;
     while (lines % segl) --segl;
-    const uint32_t KC = 256 * segl;
-    const uint32_t stage_bytes = (16 * segl * 128 + 16 * (KC / 32) * 2 + 1023) & ~1023u;
+    const uint32_t stage_bytes = (ST_ROWS * segl * 128 + ST_ROWS * segl * 16 + 1023) & ~1023u;
     const size_t xbytes = (size_t)M * K * 2 + (size_t)K;   // fragments + corr[K/32][8] floats
-    const size_t budget = 200 * 1024 - 1024;
+    const size_t budget = 188 * 1024;   // dynamic; the kernel's static shared memory is about 31 KB
     if (xbytes + 4 * (size_t)stage_bytes > budget) return cudaErrorNotSupported;
     const uint32_t nst = (uint32_t)std::min<size_t>(ST_MAX, (budget - xbytes) / stage_bytes);
     const size_t smem = 1024 + (size_t)nst * stage_bytes + xbytes;
@@ -901,7 +914,7 @@ static cudaError_t launch_int4_stream(const void* x, const void* packed, const v
     if (!stream_maps(&wm, &sm, packed, scales, N, K, segl)) return cudaErrorNotSupported;
     auto k = k_gemv_int4_stream<EPI>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const uint32_t ntiles = (N + 15) / 16;
+    const uint32_t ntiles = (N + ST_ROWS - 1) / ST_ROWS;
     const uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)gemv_sm_count());
     k<<<grid, (ST_CONS + 1) * 32, smem, s>>>(wm, sm, static_cast<const __half*>(x), static_cast<__half*>(y), M, N, K,
                               static_cast<const __half*>(norm_w), eps, segl, nst, stage_bytes, tc_error_word());
@@ -948,7 +961,7 @@ static cudaError_t gemv_int4_dispatch(const void* x, const void* packed, const v
     // several rows: the streaming kernel stages x once per SM; one row: the per-tile kernel
     // (column-block MMA) with many CTAs per SM
     if (M >= 2 && vec && aligned(packed, 16) && aligned(scales, 16) && K % 256 == 0 &&
-        N >= 16u * (uint32_t)gemv_sm_count()) {
+        N >= ST_ROWS * (uint32_t)gemv_sm_count()) {
         const cudaError_t e = launch_int4_stream<EPI>(x, packed, scales, y, M, N, K, norm_w, eps, s);
         if (e != cudaErrorNotSupported) return e;
     }
