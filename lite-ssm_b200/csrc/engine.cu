@@ -485,7 +485,7 @@ struct lssm_session {
     size_t conv_layer = 0, ssd_layer = 0;   // elements per layer
     // workspace (rows = batch * max_L)
     __half *hidden = nullptr, *normed = nullptr, *proj = nullptr, *xs = nullptr, *Bs = nullptr, *Cs = nullptr,
-           *ys = nullptr, *gated = nullptr, *mixn = nullptr, *bout = nullptr, *logits = nullptr, *lastrows = nullptr;
+           *ys = nullptr, *gated = nullptr, *mixn = nullptr, *logits = nullptr, *lastrows = nullptr;
     __half* wscratch = nullptr;   // dequantised INT4 weight for the prefill GEMM
     size_t wscratch_elems = 0;
     uint32_t *d_tokens = nullptr, *d_cur = nullptr, *d_hist = nullptr, *d_step = nullptr;
@@ -539,7 +539,7 @@ extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
     cudaStreamSynchronize(s->ctx->stream);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
-                  s->bout, s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
+                  s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
                   s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart,
                   s->d_shard, s->d_sumsq, s->d_part32, s->d_gather, s->d_cpair, s->d_pair, s->d_ticket};
     for (void* p : ps)
@@ -815,7 +815,6 @@ static lssm_status session_alloc(lssm_session* s, uint32_t batch, uint32_t max_L
     SA(s->ys, rows * s->di * 2, "session: y");
     SA(s->gated, rows * s->di * 2, "session: gated");
     SA(s->mixn, rows * s->di * 2, "session: mixer norm");
-    SA(s->bout, rows * h.d_model * 2, "session: block out");
     SA(s->logits, (size_t)batch * s->v_max * 2, "session: logits");
     SA(s->lastrows, (size_t)batch * h.d_model * 2, "session: last rows");
     SA(s->d_tokens, rows * 4, "session: tokens");
@@ -964,19 +963,14 @@ static lssm_status linear(lssm_session* s, const uint8_t* wp, uint32_t dtype, co
         s->nl += 1;
         xin = s->normed;
     }
-    const int gemm_epi = epilogue == 2 ? 0 : epilogue;
-    void* out = epilogue == 2 ? static_cast<void*>(s->bout) : y;
+    // the GEMMs apply the residual (epilogue 2) in place on y
     const void* wf = wp;
     if (dtype == DT_INT4_B32) {
         // fused dequant GEMM when the operands allow it; else dequantise to scratch + GEMM
         const void* sc = wp + (size_t)N * K / 2;
-        const cudaError_t e = launch_gemm_i4(xin, wp, sc, out, rows, N, K, gemm_epi, st);
+        const cudaError_t e = launch_gemm_i4(xin, wp, sc, y, rows, N, K, epilogue, st);
         if (e == cudaSuccess) {
             s->nl += 1;
-            if (epilogue == 2) {
-                CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
-                s->nl += 1;
-            }
             return LSSM_OK;
         }
         if (e != cudaErrorNotSupported) return cuda_fail(e, "linear: fused INT4 GEMM");
@@ -985,12 +979,8 @@ static lssm_status linear(lssm_session* s, const uint8_t* wp, uint32_t dtype, co
         s->nl += 1;
         wf = s->wscratch;
     }
-    CU(launch_gemm_f16(xin, wf, out, rows, N, K, gemm_epi, st));
+    CU(launch_gemm_f16(xin, wf, y, rows, N, K, epilogue, st));
     s->nl += 1;
-    if (epilogue == 2) {
-        CU(launch_add_inplace_f16(y, s->bout, rows * N, st));
-        s->nl += 1;
-    }
     return LSSM_OK;
 }
 

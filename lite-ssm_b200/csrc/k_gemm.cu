@@ -195,13 +195,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     }
                 } else if (row < M && col0 < N) {
                     __half h[32];
+                    __half* yr = Y + (uint64_t)row * ldy + col0;
+                    if (epilogue == 2) {   // residual: y = half(y + half(acc)) (mamba2_block.cpp:274-276)
+                        if (vec && col0 + 32 <= N) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(h)[j] = reinterpret_cast<const uint4*>(yr)[j];
+                        } else {
+                            for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) h[j] = yr[j];
+                        }
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         float f = __uint_as_float(v[j]);
                         if (epilogue == 1) f = silu(f);
+                        if (epilogue == 2) f = __half2float(h[j]) + __half2float(__float2half_rn(f));
                         h[j] = __float2half_rn(f);
                     }
-                    __half* yr = Y + (uint64_t)row * ldy + col0;
                     if (vec && col0 + 32 <= N) {
 #pragma unroll
                         for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yr)[j] = reinterpret_cast<uint4*>(h)[j];
@@ -260,6 +269,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __half* __restrict__ X,
                 float f = acc[i][j];
                 if (epilogue == 3) { reinterpret_cast<float*>(Y)[(uint64_t)r * N + c] = f; continue; }
                 if (epilogue == 1) f = silu(f);
+                if (epilogue == 2) f = __half2float(Y[(uint64_t)r * N + c]) + __half2float(__float2half_rn(f));
                 Y[(uint64_t)r * N + c] = __float2half_rn(f);
             }
         }

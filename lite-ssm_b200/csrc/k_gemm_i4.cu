@@ -196,13 +196,22 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
                     }
                 } else if (row < M && col0 < N) {
                     __half h[32];
+                    __half* yr = Y + (uint64_t)row * N + col0;
+                    if (epilogue == 2) {   // residual: y = half(y + half(acc)) (mamba2_block.cpp:274-276)
+                        if (vec && col0 + 32 <= N) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(h)[j] = reinterpret_cast<const uint4*>(yr)[j];
+                        } else {
+                            for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) h[j] = yr[j];
+                        }
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         float f = __uint_as_float(v[j]);
                         if (epilogue == 1) f = silu(f);
+                        if (epilogue == 2) f = __half2float(h[j]) + __half2float(__float2half_rn(f));
                         h[j] = __float2half_rn(f);
                     }
-                    __half* yr = Y + (uint64_t)row * N + col0;
                     if (vec && col0 + 32 <= N) {
 #pragma unroll
                         for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yr)[j] = reinterpret_cast<uint4*>(h)[j];
