@@ -182,10 +182,13 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
     // Fully unrolled over the warp's (at most MAXB) blocks so their load -> dequant ->
     // mma chains overlap: at one CTA per SM the GEMV is latency-bound otherwise.
     constexpr uint32_t MAXB = (SEG_MAX * 8 + CONS_WARPS - 1) / CONS_WARPS;
+    // Predicated rather than exited early: every iteration reads a valid block (past-the-end
+    // ones re-read block b0 with a zero scale), so the loads of all blocks can be issued
+    // ahead of the arithmetic.
 #pragma unroll
     for (uint32_t i = 0; i < MAXB; ++i) {
-        const uint32_t b = b0 + i;
-        if (b >= b1) break;
+        const bool live = b0 + i < b1;
+        const uint32_t b = live ? b0 + i : b0;
         const uint32_t s = b >> 3;
         const uint32_t off = (s << 7) + (((b & 7) ^ ((sw + s) & 7)) << 4);
         const uint4 xf = has_x ? xrow[b * 4] : make_uint4(0, 0, 0, 0);
@@ -199,7 +202,7 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
         const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
         mma_16816(d, a1, xf.x, xf.y);
         mma_16816(d, a2, xf.z, xf.w);
-        const float fa = __half2float(sa[b]), fb = __half2float(sbp[b]);
+        const float fa = live ? __half2float(sa[b]) : 0.0f, fb = live ? __half2float(sbp[b]) : 0.0f;
         acc[0] += d[0] * fa;
         acc[1] += d[1] * fa;
         acc[2] += d[2] * fb;
