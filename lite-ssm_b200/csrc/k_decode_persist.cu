@@ -222,15 +222,17 @@ __device__ __forceinline__ void consume_f16(const uint8_t* stage, uint32_t seg, 
     constexpr uint32_t MAXK = (SEG_MAX * 4 + CONS_WARPS - 1) / CONS_WARPS;
 #pragma unroll
     for (uint32_t i = 0; i < MAXK; ++i) {
-        const uint32_t ks = k0 + i;
-        if (ks >= k1) break;
+        // predicated like consume_int4: past-the-end steps re-read step k0 with a zero activation
+        const bool live = k0 + i < k1;
+        const uint32_t ks = live ? k0 + i : k0;
         const uint32_t s = ks >> 2, j = (ks & 3) * 2;
         const uint32_t a[4] = {*reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j) + 4 * c),
                                *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j) + 4 * c),
                                *reinterpret_cast<const uint32_t*>(stage + swz(g, seg, s, j + 1) + 4 * c),
                                *reinterpret_cast<const uint32_t*>(stage + swz(g + 8, seg, s, j + 1) + 4 * c)};
-        const uint32_t xb0 = has_x ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c) : 0u;
-        const uint32_t xb1 = has_x ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c + 8) : 0u;
+        const bool xv = has_x && live;
+        const uint32_t xb0 = xv ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c) : 0u;
+        const uint32_t xb1 = xv ? *reinterpret_cast<const uint32_t*>(xr + ks * 16 + 2 * c + 8) : 0u;
         mma_16816(acc, a, xb0, xb1);
     }
 }
