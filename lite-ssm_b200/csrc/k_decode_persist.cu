@@ -546,14 +546,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
                 for (uint32_t l = 0; l < p.n_layer && ok; ++l) {
                     const CUtensorMap* mp = maps + 4 * l;
-                    for (uint32_t ti = 0; ti < ntA && ok; ++ti)
-                        for (uint32_t c = 0; c < nchA && ok; ++c) {
-                            ok = put_int4(mp, p.seg_in, (cta + ti * G) * nchA + c, nchA);
-                            if (p.trace && step == 0 && ti == 0 && c == 0)
-                                p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
-                        }
-                    if (!ok) break;
-                    // this layer's ssd state rows, once the previous layer's are released
+                    // this layer's ssd state rows, as soon as the previous layer's are released
+                    // (ahead of this layer's weights, so the state lands long before phase B)
                     if (!mbar_wait_ab(smem_u32(sempty), sphase ^ 1, abort)) { ok = false; break; }
                     if (sbytes) {
                         mbar_expect(smem_u32(sfull), sbytes);
@@ -563,6 +557,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     }
                     state_issued = true;
                     sphase ^= 1;
+                    for (uint32_t ti = 0; ti < ntA && ok; ++ti)
+                        for (uint32_t c = 0; c < nchA && ok; ++c) {
+                            ok = put_int4(mp, p.seg_in, (cta + ti * G) * nchA + c, nchA);
+                            if (p.trace && step == 0 && ti == 0 && c == 0)
+                                p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
+                        }
+                    if (!ok) break;
                     for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, p.seg_out, cta + i * G, nchC);
                 }
                 const CUtensorMap* ml = maps + 4 * p.n_layer;
