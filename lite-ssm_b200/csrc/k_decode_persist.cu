@@ -78,8 +78,8 @@ constexpr uint32_t OFF_PART = OFF_X + XBUF;
 constexpr uint32_t OFF_S = OFF_PART + PART;
 constexpr uint32_t OFF_H = OFF_S + SBUF;
 constexpr uint32_t OFF_BC = OFF_H + HBUF;                 // BSLOTS x {B, C} x 128 halves
-constexpr uint32_t OFF_ROWV = OFF_BC + BSLOTS * 512;      // SROWS x 5 floats
-constexpr uint32_t OFF_RSLOT = OFF_ROWV + SROWS * 5 * 4;  // SROWS slot ids + BSLOTS (seq, group) keys
+constexpr uint32_t OFF_ROWV = OFF_BC + BSLOTS * 512;      // SROWS x 6 words: 5 per-layer floats + row info
+constexpr uint32_t OFF_RSLOT = OFF_ROWV + SROWS * 6 * 4;  // SROWS slot ids + BSLOTS (seq, group) keys
 constexpr uint32_t OFF_LT = OFF_RSLOT + 128;              // layer table
 constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
@@ -469,7 +469,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
-    if (p.dconv > 4 || p.dconv < 1 || p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || (srows + G - 1) / G > SROWS ||
+    if (p.dconv > 4 || p.dconv < 1 || p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
+        (srows + G - 1) / G > SROWS ||
         p.n_layer > LT_MAX || (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || (uint64_t)p.B * p.dm * 2 > HBUF ||
         p.dm / 8 > 3 * CONS || p.di / 8 > 3 * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
@@ -498,6 +499,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 skey[ns++] = key;
             }
             rslot[j] = (uint8_t)sl;
+            // (seq m, head h, channel pp) of the row, packed once: no divisions in phase B
+            const uint32_t m = mh / p.H, h = mh % p.H, pp = (r0 + j) % p.P;
+            reinterpret_cast<uint32_t*>(rowv)[j * 6 + 5] = (m << 24) | (pp << 16) | h;
         }
         *nslot_s = ns;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -727,12 +731,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         __ldcg(reinterpret_cast<const uint2*>(src));
                 }
                 if (tid < nrows) {
-                    const uint32_t row = r0 + tid, pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
+                    const uint32_t info = reinterpret_cast<const uint32_t*>(rowv)[tid * 6 + 5];
+                    const uint32_t m = info >> 24, pp = (info >> 16) & 0xFF, h = info & 0xFFFF;
                     const float A = -expf(__half2float(L.A_log[h]));
                     const float dt = fminf(fmaxf(softplus(__half2float(__ldcg(p.projb + (uint64_t)m * p.proj + p.di + p.xd + h)) +
                                                           __half2float(L.dt_bias[h])), 1e-6f), 1e6f);
                     const float xv = __half2float(__ldcg(p.xs + (uint64_t)m * p.di + h * p.P + pp));
-                    float* rv = rowv + tid * 5;
+                    float* rv = rowv + tid * 6;
                     rv[0] = expf(A * dt);
                     rv[1] = dt * xv;
                     rv[2] = __half2float(L.D[h]);
@@ -749,7 +754,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     for (int q = 0; q < 2; ++q) {
                         const uint32_t j = min(j0 + q * CONS_WARPS, nrows - 1);
                         const __half* bv = bcs + rslot[j] * 256;
-                        const float* rv = rowv + j * 5;
+                        const float* rv = rowv + j * 6;
                         const uint2 bu = *reinterpret_cast<const uint2*>(bv + lane * 4);
                         const uint2 cu = *reinterpret_cast<const uint2*>(bv + 128 + lane * 4);
                         const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&bu.x));
@@ -777,8 +782,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         const uint32_t row = r0 + j;
                         *reinterpret_cast<float4*>(L.ssd_state + (uint64_t)row * p.N + lane * 4) = v2[q];
                         if (lane == 0) {
-                            const float* rv = rowv + j * 5;
-                            const uint32_t pp = row % p.P, mh = row / p.P, m = mh / p.H, h = mh % p.H;
+                            const float* rv = rowv + j * 6;
+                            const uint32_t info = reinterpret_cast<const uint32_t*>(rv)[5];
+                            const uint32_t m = info >> 24, pp = (info >> 16) & 0xFF, h = info & 0xFFFF;
                             const float yh = __half2float(__float2half_rn(a2[q] + rv[2] * rv[3]));
                             p.gated[(uint64_t)m * p.di + h * p.P + pp] = __float2half_rn(silu(rv[4]) * yh);
                         }
@@ -932,7 +938,8 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     const uint32_t G = sh.sm_count;
     if (sh.B < 1 || sh.B > 2) return "batch must be 1 or 2";
     if (sh.N != 128) return "d_state must be 128";
-    if (sh.P < 32) return "d_head must be >= 32";
+    if (sh.P < 32 || sh.P > 256) return "d_head must be 32..256";
+    if (sh.H > 65535) return "more than 65535 heads";
     if (sh.dconv < 1 || sh.dconv > 4) return "d_conv must be 1..4";
     if (sh.dm % 256 || sh.di % 256) return "d_model and d_inner must be multiples of 256";
     if (sh.dm / 8 > 3 * CONS || sh.di / 8 > 3 * CONS) return "d_model / d_inner too wide for the staged RMSNorm";
