@@ -523,25 +523,38 @@ def run_kernel_bench(args):
         b = X.numel() * 2 + Bm.numel() * 2 * 2 + dt.numel() * 4 + Y.numel() * 4 + 2 * S.numel() * 4
         out.update(shape=[Bt, Ls, H, P, N], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
     elif args.kernel == "ssd_step":
-        H, P, N, nl = 80, 64, 128, 64
-        S = torch.zeros(nl, H, P, N, device=dev)
-        x = torch.randn(H * P, device=dev, generator=g).half()
-        Bm = torch.randn(N, device=dev, generator=g).half()
-        Cm = torch.randn(N, device=dev, generator=g).half()
-        dt = torch.randn(H, device=dev, generator=g).half()
+        H, P, N = 80, 64, 128
+        Bt = args.step_batch
+        per = Bt * H * P * N                   # state floats per slice
+        nl = max(2, min(64, int(2e9 // (per * 4))))
+        S = torch.zeros(nl * per, device=dev)
+        x = torch.randn(Bt * H * P, device=dev, generator=g).half()
+        Bm = torch.randn(Bt * N, device=dev, generator=g).half()
+        Cm = torch.randn(Bt * N, device=dev, generator=g).half()
+        dt = torch.randn(Bt * H, device=dev, generator=g).half()
         par = torch.zeros(H, device=dev).half()
-        y = torch.empty(H * P, device=dev, dtype=torch.half)
+        y = torch.empty(Bt * H * P, device=dev, dtype=torch.half)
         torch.cuda.synchronize()
-        dims = lssm.SSDStepDims(H, P, N, 1, 1e-6, 1e6, 1)
+        if Bt == 1:
+            dims = lssm.SSDStepDims(H, P, N, 1, 1e-6, 1e6, 1)
 
-        def call(i):
-            so = (i % nl) * H * P * N * 4
-            lssm.check(L.lssm_ssd_step_f16(ctx.h, x.data_ptr(), 0, Bm.data_ptr(), 0, Cm.data_ptr(), 0, dt.data_ptr(), 0,
-                                           par.data_ptr(), 0, par.data_ptr(), 0, par.data_ptr(), 0, S.data_ptr(), so,
-                                           y.data_ptr(), 0, dims))
+            def call(i):
+                so = (i % nl) * per * 4
+                lssm.check(L.lssm_ssd_step_f16(ctx.h, x.data_ptr(), 0, Bm.data_ptr(), 0, Cm.data_ptr(), 0, dt.data_ptr(),
+                                               0, par.data_ptr(), 0, par.data_ptr(), 0, par.data_ptr(), 0, S.data_ptr(),
+                                               so, y.data_ptr(), 0, dims))
+        else:
+            bdims = lssm.SSDBatchedDims(Bt, 1, H, P, N, 1, 256, 1e-6, 1e6, 1, 0, 0, 0, 0)
+
+            def call(i):
+                lssm.check(L.lssm_ssd_step_batched(ctx.h, x.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), dt.data_ptr(),
+                                                   par.data_ptr(), par.data_ptr(), par.data_ptr(),
+                                                   S.data_ptr() + (i % nl) * per * 4, y.data_ptr(), bdims))
+        call(0)
+        torch.cuda.synchronize()
         ms = timed(call, reps)
-        b = 2 * H * P * N * 4 + H * P * 4
-        out.update(shape=[H, P, N], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
+        b = 2 * per * 4 + Bt * H * P * 4
+        out.update(shape=[Bt, H, P, N], us=ms * 1e3, bytes=b, gbs=b / ms / 1e6, frac=b / ms / 1e6 / hbm)
     out["peak"] = f"{peak_kind} (hbm {hbm} GB/s, bf16 {tflops} TF/s)"
     print(json.dumps(out), flush=True)
     _ = C
@@ -750,6 +763,7 @@ def main():
     ap.add_argument("--n", type=int, default=10576)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--ssd-batch", type=int, default=8)
+    ap.add_argument("--step-batch", type=int, default=1, help="sequences of the ssd_step microbenchmark")
     ap.add_argument("--ssd-len", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)

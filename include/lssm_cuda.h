@@ -205,6 +205,13 @@ typedef struct {
 lssm_status lssm_ssd_chunked_batched(lssm_ctx* ctx, const void* X, const void* B, const void* C,
                                      const void* dt_raw, const void* dt_bias, const void* A_log,
                                      const void* D_skip, void* Y, void* state_io, lssm_ssd_batched_dims dims);
+/* Batched-decode extension of ssd_step (ops.hpp:227-236 takes one sequence): one decode token of
+ * dims.batch sequences, fp16 x (batch, H*P), B / C (batch, n_groups*N), dt_raw (batch, H), fp16
+ * dt_bias / A_log / D (H), fp32 state_io (batch, H, P, N) updated in place, fp16 y (batch, H*P).
+ * Uses dims.batch, H, P, N, n_groups, dt_min, dt_max, has_D; the dtype fields are ignored. */
+lssm_status lssm_ssd_step_batched(lssm_ctx* ctx, const void* x, const void* B, const void* C, const void* dt_raw,
+                                  const void* dt_bias, const void* A_log, const void* D_skip, void* state_io,
+                                  void* y, lssm_ssd_batched_dims dims);
 
 /* ---- engine: .ssm model + session (the callers of the ops: src/model/*.cpp, src/runtime/*.cpp) ---- */
 typedef struct lssm_model lssm_model;

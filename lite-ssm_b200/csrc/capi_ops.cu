@@ -502,4 +502,22 @@ lssm_status lssm_ssd_chunked_batched(lssm_ctx* ctx, const void* X, const void* B
     LAUNCH("ssd_chunked_batched", launch_ssd_chunked(a, ctx->stream));
 }
 
+lssm_status lssm_ssd_step_batched(lssm_ctx* ctx, const void* x, const void* B, const void* C, const void* dt_raw,
+                                  const void* dt_bias, const void* A_log, const void* D_skip, void* state_io, void* y,
+                                  lssm_ssd_batched_dims d) {
+    CHECK_CTX(ctx);
+    if (!d.batch || !d.H || !d.P || !d.N) return LSSM_OK;
+    const uint32_t G = d.n_groups ? d.n_groups : 1;
+    if (d.H % G) return fail(LSSM_ERR_INVALID_ARGUMENT, "ssd_step_batched: n_heads must be a multiple of n_groups");
+    StepArgs a{};
+    a.x = static_cast<const __half*>(x); a.B = static_cast<const __half*>(B); a.C = static_cast<const __half*>(C);
+    a.dt_raw = static_cast<const __half*>(dt_raw); a.dt_bias = static_cast<const __half*>(dt_bias);
+    a.A_log = static_cast<const __half*>(A_log); a.D = static_cast<const __half*>(D_skip);
+    a.state = static_cast<float*>(state_io); a.y = static_cast<__half*>(y); a.z = nullptr;
+    a.batch = d.batch; a.H = d.H; a.P = d.P; a.N = d.N; a.G = G;
+    a.dt_min = d.dt_min; a.dt_max = d.dt_max; a.has_D = d.has_D;
+    a.x_bs = (uint64_t)d.H * d.P; a.bc_bs = (uint64_t)G * d.N; a.dt_bs = d.H; a.y_bs = (uint64_t)d.H * d.P; a.z_bs = 0;
+    LAUNCH("ssd_step_batched", launch_ssd_step_ex(a, ctx->stream));
+}
+
 }  // extern "C"

@@ -94,6 +94,7 @@ _SIGS = {
     "lssm_linear_int4_gemv": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
     "lssm_linear_int4_gemv_rows": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
     "lssm_linear_f16_gemv_rows": [P, P, sz, P, sz, P, sz, LinearDims],
+    "lssm_ssd_step_batched": [P, P, P, P, P, P, P, P, P, P, SSDBatchedDims],
     "lssm_linear_int4_gemm": [P, P, sz, P, sz, P, sz, P, sz, LinearDims],
     "lssm_silu_f16": [P, P, sz, P, sz, u32],
     "lssm_add_inplace_f16": [P, P, sz, P, sz, u32],

@@ -312,6 +312,31 @@ def test_ssd_step(ctx, ops, H, P, N, G):
     close(get16(by, H * P), po.to_f32(ry), rtol=1e-2, atol=2e-3)
 
 
+@pytest.mark.parametrize("Bt,H,P,N,G", [(5, 80, 64, 128, 1), (3, 16, 64, 128, 8), (2, 6, 16, 16, 2)])
+def test_ssd_step_batched(ctx, Bt, H, P, N, G):
+    """Batched-decode extension: each sequence against the oracle's one-sequence ssd_step."""
+    ins = [_ssd_inputs(1, H, P, N, G, seed=10 + b) for b in range(Bt)]
+    S = (RNG.standard_normal((Bt, H, P, N)) * 0.3).astype(np.float32)
+    rS, ry = S.copy(), np.zeros((Bt, H * P), np.uint16)
+    for b in range(Bt):
+        X, Bm, Cm, dt, db, alog, D = ins[b]
+        sb = np.ascontiguousarray(rS[b])
+        yb = np.zeros(H * P, np.uint16)
+        po.lib().lssm_oracle_ssd_step_f16(*(po.ptr(a.view(np.uint16)) for a in (X, Bm, Cm, dt, ins[0][4], ins[0][5],
+                                                                                 ins[0][6])), po.ptr(sb), po.ptr(yb),
+                                          H, P, N, G, 1e-6, 1e6, 1)
+        rS[b], ry[b] = sb, yb
+    cat = lambda k: np.ascontiguousarray(np.concatenate([ins[b][k].ravel() for b in range(Bt)]))  # noqa: E731
+    bx, bB, bC, bdt = (hb(ctx, cat(k)) for k in (0, 1, 2, 3))
+    bdb, bal, bD = (hb(ctx, ins[0][k]) for k in (4, 5, 6))
+    bS, by = hb(ctx, S), lssm.DeviceBuffer(ctx, Bt * H * P * 2)
+    dims = lssm.SSDBatchedDims(Bt, 1, H, P, N, G, 256, 1e-6, 1e6, 1, 0, 0, 0, 0)
+    lssm.check(lssm.lib().lssm_ssd_step_batched(ctx.h, bx.ptr, bB.ptr, bC.ptr, bdt.ptr, bdb.ptr, bal.ptr, bD.ptr,
+                                                bS.ptr, by.ptr, dims))
+    close(bS.download(np.float32, Bt * H * P * N).reshape(Bt, H, P, N), rS, rtol=1e-5, atol=1e-5)
+    close(get16(by, Bt * H * P).reshape(Bt, H * P), po.to_f32(ry), rtol=1e-2, atol=2e-3)
+
+
 @pytest.mark.parametrize("L,H,P,N,G,chunk", [(77, 8, 64, 128, 1, 64), (40, 6, 16, 16, 2, 16), (1, 4, 8, 8, 1, 256),
                                              (300, 4, 64, 128, 1, 256)])
 def test_ssd_chunked_f16(ctx, ops, L, H, P, N, G, chunk):
