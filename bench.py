@@ -174,6 +174,8 @@ def graph_timed(ctx, stream, call, n, replays=4):
     once into a CUDA graph through the library's graph batching and the graph is
     replayed, so the CUDA events measure kernels back to back, not host submission."""
     import torch
+    call(0)                            # eager first call: loads kernels, sizes scratch outside capture
+    torch.cuda.synchronize()
     ctx.set_graph_batching(True)
     try:
         ctx.begin_batch()
