@@ -368,8 +368,13 @@ lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, co
     if (d.K % 32 != 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "linear_int4_gemm: K must be a multiple of 32");
     if (d.M == 0 || d.N == 0) return finish_op(ctx, "linear_int4_gemm");
     {
+        // decode-size M may split K over CTAs: fp32 partials (up to 8 splits) in the scratch
+        void* ws = nullptr;
+        const size_t ws_bytes = d.M <= 128 ? (size_t)8 * d.M * d.N * 4 : 0;
+        if (ws_bytes)
+            if (lssm_status st = scratch_reserve(ctx, ws_bytes, &ws)) return st;
         const cudaError_t e = launch_gemm_i4(bp(x, x_off), bp(w, w_packed_off), bp(w_scl, w_scales_off), bp(y, y_off),
-                                             d.M, d.N, d.K, 0, ctx->stream);
+                                             d.M, d.N, d.K, 0, ctx->stream, static_cast<float*>(ws), ws_bytes);
         if (e != cudaErrorNotSupported) {
             if (e != cudaSuccess) return cuda_fail(e, "linear_int4_gemm");
             return finish_op(ctx, "linear_int4_gemm");

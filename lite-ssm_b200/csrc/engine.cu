@@ -968,9 +968,12 @@ static lssm_status linear(lssm_session* s, const uint8_t* wp, uint32_t dtype, co
     if (dtype == DT_INT4_B32) {
         // fused dequant GEMM when the operands allow it; else dequantise to scratch + GEMM
         const void* sc = wp + (size_t)N * K / 2;
-        const cudaError_t e = launch_gemm_i4(xin, wp, sc, y, rows, N, K, epilogue, st);
+        // the dequant scratch is idle on this path: it holds the split-K partials
+        int launched = 0;
+        const cudaError_t e = launch_gemm_i4(xin, wp, sc, y, rows, N, K, epilogue, st,
+                                             reinterpret_cast<float*>(s->wscratch), s->wscratch_elems * 2, &launched);
         if (e == cudaSuccess) {
-            s->nl += 1;
+            s->nl += launched;
             return LSSM_OK;
         }
         if (e != cudaErrorNotSupported) return cuda_fail(e, "linear: fused INT4 GEMM");

@@ -69,11 +69,22 @@ __device__ __forceinline__ uint4 dequant_scaled(uint32_t w, __half2 s2) {
     return r;
 }
 
+// Work unit `tile` of m_tiles x n_tiles x splits: its (m, n) tile and K-block range. K is
+// split on 256-wide scale groups (four K blocks), so every split starts on a group.
+struct I4Unit {
+    uint32_t mb, nb, ks, kb0, kb1;
+};
+__device__ __forceinline__ I4Unit i4_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits,
+                                          uint32_t nk) {
+    const uint32_t mn = m_tiles * n_tiles, ks = tile / mn, rem = tile - ks * mn, groups = nk / 4;
+    return {rem % m_tiles, rem / m_tiles, ks, 4 * (ks * groups / splits), 4 * ((ks + 1) * groups / splits)};
+}
+
 template <int BN>
 __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
     k_gemm_i4(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
               const __half* __restrict__ scales, __half* __restrict__ Y, uint32_t M, uint32_t N, uint32_t K,
-              int epilogue, int* __restrict__ err) {
+              int epilogue, uint32_t splits, float* __restrict__ ws, int* __restrict__ err) {
     using Cfg = I4Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -92,7 +103,7 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t m_tiles = (M + I4_BM - 1) / I4_BM, n_tiles = (N + BN - 1) / BN;
-    const uint32_t ntiles = m_tiles * n_tiles, nk = K / I4_BK;
+    const uint32_t ntiles = m_tiles * n_tiles * splits, nk = K / I4_BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -122,8 +133,9 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
             int last_phase[Cfg::STAGES];
             for (int s = 0; s < Cfg::STAGES; ++s) last_phase[s] = -1;
             for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-                const uint32_t mb = tile % m_tiles, nb = tile / m_tiles;
-                for (uint32_t kb = 0; kb < nk; ++kb) {
+                const I4Unit u = i4_unit(tile, m_tiles, n_tiles, splits, nk);
+                const uint32_t mb = u.mb, nb = u.nb;
+                for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!tc::mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag)) goto producer_done;
                     const uint32_t fb = smem_u32(&full[stage]);
                     tc::mbar_arrive_expect_tx(fb, Cfg::A_BYTES + Cfg::Q_BYTES);
@@ -145,8 +157,9 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
                 if (!tc::mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag)) break;
                 tc::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
+                const I4Unit u = i4_unit(tile, m_tiles, n_tiles, splits, nk);
                 bool ok = true;
-                for (uint32_t kb = 0; kb < nk; ++kb) {
+                for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!tc::mbar_wait(smem_u32(&full[stage]), phase, abort_flag) ||
                         !tc::mbar_wait(smem_u32(&bready[stage]), phase, abort_flag)) {
                         ok = false;
@@ -157,7 +170,7 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
                     const uint64_t db = tc::sw128_kmajor_desc(smem_u32(sB + stage * Cfg::B_BYTES));
 #pragma unroll
                     for (uint32_t k = 0; k < I4_BK / 16; ++k)
-                        tc::umma_f16(d_tmem, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
+                        tc::umma_f16(d_tmem, da + 2 * k, db + 2 * k, IDESC, (kb != u.kb0) || k != 0);
                     tc::umma_commit(smem_u32(&empty[stage]));
                     if (++stage == (uint32_t)Cfg::STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -174,8 +187,12 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
         const uint32_t q = warp & 3;
         uint32_t acc = 0, acc_phase = 0;
         const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
+        // split K: fp32 partials of split ks to ws[ks][M][N] (16-byte aligned), summed afterwards
+        const bool part = splits > 1;
+        const bool vecf = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(part ? (void*)ws : (void*)Y) & 15) == 0);
         for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            const uint32_t mb = tile % m_tiles, nb = tile / m_tiles;
+            const I4Unit u = i4_unit(tile, m_tiles, n_tiles, splits, nk);
+            const uint32_t mb = u.mb, nb = u.nb;
             if (!tc::mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag)) break;
             tc::tc_fence_after();
             const uint32_t row = mb * I4_BM + q * 32 + lane;
@@ -185,10 +202,10 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
                 tc::tmem_ld32(tmem_base + acc * BN + ch * 32 + ((q * 32) << 16), v);
                 tc::tmem_ld_wait();
                 const uint32_t col0 = nb * BN + ch * 32;
-                if (row < M && col0 < N && epilogue == 3) {
-                    // fp32 output (partial sums that a collective adds before rounding)
-                    float* yf = reinterpret_cast<float*>(Y) + (uint64_t)row * N + col0;
-                    if (vec && col0 + 32 <= N && (N % 4 == 0)) {
+                if (row < M && col0 < N && (epilogue == 3 || part)) {
+                    // fp32 output (partial sums that a collective, or the split-K sum, adds before rounding)
+                    float* yf = (part ? ws + (uint64_t)u.ks * M * N : reinterpret_cast<float*>(Y)) + (uint64_t)row * N + col0;
+                    if (vecf && col0 + 32 <= N) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(yf)[j] = reinterpret_cast<uint4*>(v)[j];
                     } else {
@@ -233,15 +250,17 @@ __global__ void __launch_bounds__(I4Cfg<BN>::THREADS, 1)
         uint32_t stage = 0, phase = 0;
         const uint32_t nsc = K / 256;   // 16-byte scale groups (8 blocks) per row
         for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            const uint32_t nb = tile / m_tiles, n = nb * BN + r;
+            const I4Unit u = i4_unit(tile, m_tiles, n_tiles, splits, nk);
+            const uint32_t nb = u.nb, n = nb * BN + r;
             const bool valid = n < N;
             const uint4* srow = reinterpret_cast<const uint4*>(scales + (uint64_t)(valid ? n : 0) * (K / 32));
             const uint4 zero4 = make_uint4(0, 0, 0, 0);
-            uint4 cur = valid ? __ldg(srow) : zero4;
-            uint4 nxt = (valid && nsc > 1) ? __ldg(srow + 1) : zero4;
+            const uint32_t g0 = u.kb0 >> 2;
+            uint4 cur = valid ? __ldg(srow + g0) : zero4;
+            uint4 nxt = (valid && g0 + 1 < nsc) ? __ldg(srow + g0 + 1) : zero4;
             bool ok = true;
-            for (uint32_t kb = 0; kb < nk; ++kb) {
-                if ((kb & 3) == 0 && kb) {
+            for (uint32_t kb = u.kb0; kb < u.kb1; ++kb) {
+                if ((kb & 3) == 0 && kb != u.kb0) {
                     cur = nxt;
                     const uint32_t g = (kb >> 2) + 1;
                     nxt = (valid && g < nsc) ? __ldg(srow + g) : zero4;
@@ -288,9 +307,40 @@ bool make_tmap_q(CUtensorMap* map, const void* base, uint32_t N, uint32_t K, uin
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// y = epilogue(sum over the splits of the fp32 partials ws[split][M][N]), four columns per
+// thread, splits added in order: the same epilogues as the GEMM's own (0 fp16, 1 SiLU,
+// 2 residual y = half(y + half(acc)), 3 fp32).
+__global__ void k_splitk_reduce(const float* __restrict__ ws, uint32_t splits, uint64_t mn, void* __restrict__ Y,
+                                int epilogue) {
+    const uint64_t i = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i >= mn) return;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t nv = mn - i < 4 ? (uint32_t)(mn - i) : 4;
+    if (nv == 4 && (mn & 3) == 0) {
+        for (uint32_t k = 0; k < splits; ++k) {
+            const float4 p = *reinterpret_cast<const float4*>(ws + k * mn + i);
+            a[0] += p.x; a[1] += p.y; a[2] += p.z; a[3] += p.w;
+        }
+    } else {
+        for (uint32_t k = 0; k < splits; ++k)
+            for (uint32_t j = 0; j < nv; ++j) a[j] += ws[k * mn + i + j];
+    }
+    if (epilogue == 3) {
+        for (uint32_t j = 0; j < nv; ++j) static_cast<float*>(Y)[i + j] = a[j];
+        return;
+    }
+    __half* y = static_cast<__half*>(Y) + i;
+    for (uint32_t j = 0; j < nv; ++j) {
+        float f = a[j];
+        if (epilogue == 1) f = silu(f);
+        if (epilogue == 2) f = __half2float(y[j]) + __half2float(__float2half_rn(f));
+        y[j] = __float2half_rn(f);
+    }
+}
+
 template <int BN>
 cudaError_t run_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
-                        uint32_t K, int epilogue, int sms, cudaStream_t s) {
+                        uint32_t K, int epilogue, int sms, cudaStream_t s, uint32_t splits = 1, float* ws = nullptr) {
     using Cfg = I4Cfg<BN>;
     CUtensorMap ta, tq;
     if (!make_tmap_2d_k64(&ta, x, M, K, K, I4_BM, CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
@@ -298,10 +348,18 @@ cudaError_t run_gemm_i4(const void* x, const void* packed, const void* scales, v
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_gemm_i4<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return e;
-    const uint32_t tiles = ((M + I4_BM - 1) / I4_BM) * ((N + BN - 1) / BN);
+    const uint32_t tiles = ((M + I4_BM - 1) / I4_BM) * ((N + BN - 1) / BN) * splits;
     const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
     k_gemm_i4<BN><<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tq, static_cast<const __half*>(scales),
-                                                         static_cast<__half*>(y), M, N, K, epilogue, tc_error_word());
+                                                         static_cast<__half*>(y), M, N, K, epilogue, splits, ws,
+                                                         tc_error_word());
+    if (splits > 1) {
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        const uint64_t mn = (uint64_t)M * N;
+        const uint64_t threads = (mn + 3) / 4;
+        k_splitk_reduce<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(ws, splits, mn, y, epilogue);
+    }
     return cudaGetLastError();
 }
 
@@ -310,30 +368,61 @@ cudaError_t run_gemm_i4(const void* x, const void* packed, const void* scales, v
 // Fused INT4 GEMM for the small-M (batched decode) shapes where it beats dequantising
 // once: returns cudaErrorNotSupported otherwise, or when the operands do not fit the TMA
 // path (K % 256, 16-byte alignment of x / packed / scales); the caller then falls back
-// to dequantise-then-GEMM.
+// to dequantise-then-GEMM. `ws` (`ws_bytes`, 16-byte aligned, may be null) lets M <= 128
+// split K over CTAs; `launches` (may be null) receives the number of kernels launched.
 cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
-                           uint32_t K, int epilogue, cudaStream_t s) {
+                           uint32_t K, int epilogue, cudaStream_t s, float* ws, size_t ws_bytes, int* launches) {
+    if (launches) *launches = 0;
     if (!M || !N || !K) return cudaSuccess;
     if (K % 256 || !aligned(x, 16) || !aligned(packed, 16) || !aligned(scales, 16)) return cudaErrorNotSupported;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (M > 512) return cudaErrorNotSupported;
+    const uint32_t mt = (M + I4_BM - 1) / I4_BM;
+    const int cands[3] = {256, 128, 64};
+    if (M <= 128 && ws && aligned(ws, 16)) {
+        // Decode-size M has few (m, n) tiles, and each walks all of K at ~0.4-0.75 us per
+        // 64-wide K block (the 3-, 5- and 6-stage rings of BN 256 / 128 / 64): split K over
+        // 256-wide groups so the tiles x splits fill the SMs, fp32 partials in ws, then one
+        // summing pass (~2 us).
+        const uint32_t groups = K / 256;
+        double best = 1e30;
+        int best_bn = 128;
+        uint32_t best_s = 1;
+        for (int c : cands) {
+            const uint32_t base = mt * ((N + c - 1) / c);
+            uint32_t sp = base >= (uint32_t)sms ? 1 : (uint32_t)sms / base;
+            if (sp > groups) sp = groups;
+            if (sp > 8) sp = 8;
+            while (sp > 1 && (size_t)sp * M * N * 4 > ws_bytes) --sp;
+            const uint32_t waves = (base * sp + sms - 1) / sms;
+            const double tblk = c >= 256 ? 0.75 : (c >= 128 ? 0.45 : 0.4);
+            const double cost = waves * ((groups + sp - 1) / sp) * 4 * tblk + (sp > 1 ? 2.0 : 0.0);
+            if (cost < best - 1e-9) { best = cost; best_bn = c; best_s = sp; }
+        }
+        if (best_s > 1) {
+            if (launches) *launches = 2;
+            if (best_bn == 256) return run_gemm_i4<256>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
+            if (best_bn == 128) return run_gemm_i4<128>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
+            return run_gemm_i4<64>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
+        }
+    }
     // Each M tile re-dequantises its weights: beyond a few M tiles, dequantising once and
     // running the fp16 GEMM is cheaper (2048 x 10576 x 2560: 148 vs 166 us); and with too
     // few N tiles to fill half the SMs the per-tile K loop is exposed. Both go to the caller's
     // dequantise-then-GEMM path.
-    if (M > 512 || (N + 63) / 64 < (uint32_t)sms / 2) return cudaErrorNotSupported;
+    if ((N + 63) / 64 < (uint32_t)sms / 2) return cudaErrorNotSupported;
     // N tile with the fewest idle SM-slots over the persistent waves (small M: more tiles)
-    const uint32_t mt = (M + I4_BM - 1) / I4_BM;
     double best = -1.0;
     int best_bn = 128;
-    const int cands[3] = {256, 128, 64};
     for (int c : cands) {
         const uint32_t tiles = mt * ((N + c - 1) / c);
         const uint32_t waves = (tiles + sms - 1) / sms;
         const double eff = (double)M * N / ((double)waves * sms * I4_BM * c);
         if (eff > best + 1e-9) { best = eff; best_bn = c; }
     }
+    if (launches) *launches = 1;
     if (best_bn == 256) return run_gemm_i4<256>(x, packed, scales, y, M, N, K, epilogue, sms, s);
     if (best_bn == 128) return run_gemm_i4<128>(x, packed, scales, y, M, N, K, epilogue, sms, s);
     return run_gemm_i4<64>(x, packed, scales, y, M, N, K, epilogue, sms, s);

@@ -84,7 +84,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // One-time per-device setup of the GEMV kernels (shared-memory limits), from context creation.
 void gemv_init();
 cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
-                           uint32_t K, int epilogue, cudaStream_t s);
+                           uint32_t K, int epilogue, cudaStream_t s, float* ws = nullptr, size_t ws_bytes = 0,
+                           int* launches = nullptr);
 
 cudaError_t launch_ssd_step(const void* x, const void* B, const void* C, const void* dt_raw, const void* dt_bias,
                             const void* A_log, const void* D, float* state, void* y, uint32_t batch, uint32_t H,

@@ -122,6 +122,24 @@ def test_synthesized_batch4_vs_oracle(ctx):
         assert near_tie_ok(toks[b], otoks, np.concatenate([opre[None], ostep]))
 
 
+def test_synthesized_batch16_split_gemm_vs_oracle(ctx):
+    """Batch-16 decode: 16 rows take the fused INT4 GEMM, which at this M splits K over CTAs
+    (in_proj 5288 x 1280, out_proj 1280 x 2560 with the residual applied by the split-K sum);
+    each sequence against the oracle."""
+    hp = dict(d_model=1280, n_layer=2, d_state=64, d_conv=4, expand=2, vocab_size=512, n_heads=40, d_head=64,
+              chunk_size=64, n_groups=1, norm_before_gate=0)
+    m = lssm.Model.synthesize(ctx, lssm.hparams(**hp), seed=7, int4=True)
+    prompts = np.random.default_rng(11).integers(0, 512, size=(16, 24)).astype(np.uint32)
+    s = lssm.Session(ctx, m, batch=16, max_seq_len=24)
+    toks = s.generate(prompts, 5)
+    last = s.logits()
+    ora = po.OracleModel(m.download_bytes(), mode=0)
+    for b in range(16):
+        otoks, opre, ostep = ora.generate(prompts[b], 5, teacher=toks[b])
+        assert near_tie_ok(toks[b], otoks, np.concatenate([opre[None], ostep]))
+        assert np.abs(last[b] - ostep[-1]).max() < 0.1
+
+
 def test_engine_errors(ctx, golden):
     model = lssm.Model.load(ctx, golden / "tinyB_fp16.ssm")
     s = lssm.Session(ctx, model, batch=1, max_seq_len=8)

@@ -186,11 +186,13 @@ def test_int4_rejects_bad_dims(ctx, ops):
         ops.linear_int4_gemm((b, 0), (b, 0), (b, 0), (b, 0), lssm.LinearDims(3, 4, 48))
 
 
-# (512, 10576, 2560), (64, 5120, 5120) and (200, 4810, 768) take the fused dequant
-# tcgen05 kernel (k_gemm_i4, ragged last N tile in the last case); the others the
-# dequantise-then-GEMM path. Same fp16 rounding of each weight in both.
+# (512, 10576, 2560) and (200, 4810, 768) take the fused dequant tcgen05 kernel (k_gemm_i4,
+# ragged last N tile in the last case); M <= 128 with K >= 512 splits K over CTAs in it
+# ((64, 5120, 5120), (64, 2560, 5120), (16, 10576, 2560), (33, 1000, 768): fp32 partials
+# summed by a second kernel); the others the dequantise-then-GEMM path. Same fp16 rounding
+# of each weight in both.
 @pytest.mark.parametrize("M,N,K", [(100, 300, 256), (512, 10576, 2560), (17, 33, 96), (64, 5120, 5120),
-                                   (200, 4810, 768)])
+                                   (200, 4810, 768), (64, 2560, 5120), (16, 10576, 2560), (33, 1000, 768)])
 def test_linear_int4_gemm(ctx, ops, M, N, K):
     packed, scales = _int4_weights(N, K)
     x = h(RNG.standard_normal((M, K)))
