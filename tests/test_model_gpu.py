@@ -137,7 +137,9 @@ def test_synthesized_batch16_split_gemm_vs_oracle(ctx):
     for b in range(16):
         otoks, opre, ostep = ora.generate(prompts[b], 5, teacher=toks[b])
         assert near_tie_ok(toks[b], otoks, np.concatenate([opre[None], ostep]))
-        assert np.abs(last[b] - ostep[-1]).max() < 0.1
+        # this model's logits reach |40|, where one fp16 ulp is 0.031: a few ulps of the
+        # fp16 activations, summed in another order, on top of the 0.1 absolute budget
+        np.testing.assert_array_less(np.abs(last[b] - ostep[-1]), 0.1 + 4e-3 * np.abs(ostep[-1]))
 
 
 def test_engine_errors(ctx, golden):
