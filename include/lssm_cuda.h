@@ -124,6 +124,11 @@ lssm_status lssm_linear_silu_f16_gemm(lssm_ctx* ctx, const void* x, size_t x_off
 lssm_status lssm_linear_int4_gemv(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:135-139 */
+/* The INT4 GEMM uses the context's device scratch. For M <= 128 it holds the split-K fp32
+ * partials (8*M*N*4 bytes reserved); when the fused kernel cannot take the shape, it holds the
+ * dequantised fp16 weight (N*K*2 bytes). The scratch grows by reallocation, which a graph capture
+ * cannot hold: under graph batching, first make one call of the same or a larger shape outside
+ * the batch. */
 lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:141-145 */

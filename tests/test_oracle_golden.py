@@ -21,7 +21,9 @@ def test_fp16_conversion_matches_numpy():
                                     dtype=np.float32)]).astype(np.float32)
     ours = np.zeros(len(vals), dtype=np.uint16)
     po.lib().lssm_oracle_f32_to_f16(po.ptr(vals), po.ptr(ours), len(vals))
-    assert np.array_equal(ours, vals.astype(np.float16).view(np.uint16))
+    with np.errstate(over="ignore"):   # 65520 and the 10^4-scaled samples round to inf on purpose
+        want = vals.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, want)
     back = np.zeros(len(vals), dtype=np.float32)
     po.lib().lssm_oracle_f16_to_f32(po.ptr(ours), po.ptr(back), len(vals))
     assert np.array_equal(back, ours.view(np.float16).astype(np.float32))
