@@ -15,6 +15,11 @@
 
 #include <cmath>
 #include <cstring>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <fstream>
 #include <memory>
 #include <sstream>
@@ -209,22 +214,37 @@ static lssm_status upload_image(lssm_ctx* ctx, lssm_model* m, const uint8_t* byt
     cudaError_t e = cudaMalloc(&m->d_base, n);
     if (e != cudaSuccess) return cuda_fail(e, "lssm_model_load: weights arena");
     m->nbytes = n;
-    // Stage through pinned memory in 64 MiB pieces so the copy runs at PCIe speed.
+    // Stage through two pinned 64 MiB buffers so the copy runs at PCIe speed and the host
+    // copy of one piece overlaps the device copy of the previous one.
     const size_t piece = 64ull << 20;
-    void* pinned = nullptr;
-    if (cudaMallocHost(&pinned, piece) != cudaSuccess) pinned = nullptr;
-    for (size_t off = 0; off < n; off += piece) {
+    void* pinned[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    bool staged = true;
+    for (int i = 0; i < 2; ++i) {
+        staged = staged && cudaMallocHost(&pinned[i], piece) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) == cudaSuccess;
+    }
+    cudaGetLastError();
+    size_t k = 0;
+    for (size_t off = 0; off < n && e == cudaSuccess; off += piece, ++k) {
         const size_t len = std::min(piece, n - off);
-        if (pinned) {
-            std::memcpy(pinned, bytes + off, len);
-            e = cudaMemcpyAsync(m->d_base + off, pinned, len, cudaMemcpyHostToDevice, ctx->stream);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (staged) {
+            const int b = (int)(k & 1);
+            if (k >= 2) e = cudaEventSynchronize(done[b]);   // the copy that last used this buffer
+            if (e != cudaSuccess) break;
+            std::memcpy(pinned[b], bytes + off, len);
+            e = cudaMemcpyAsync(m->d_base + off, pinned[b], len, cudaMemcpyHostToDevice, ctx->stream);
+            if (e == cudaSuccess) e = cudaEventRecord(done[b], ctx->stream);
         } else {
             e = cudaMemcpy(m->d_base + off, bytes + off, len, cudaMemcpyHostToDevice);
         }
-        if (e != cudaSuccess) break;
     }
-    if (pinned) cudaFreeHost(pinned);
+    const cudaError_t es = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = es;
+    for (int i = 0; i < 2; ++i) {
+        if (done[i]) cudaEventDestroy(done[i]);
+        if (pinned[i]) cudaFreeHost(pinned[i]);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "lssm_model_load: upload");
     return LSSM_OK;
 }
@@ -245,15 +265,41 @@ extern "C" lssm_status lssm_model_load_bytes(lssm_ctx* ctx, const void* bytes, s
     return LSSM_OK;
 }
 
+// The file is mapped read-only as MmapFile does (src/core/allocator.cpp:31-64, same open /
+// empty-file errors), parsed and validated in place, and streamed to HBM from the mapping,
+// with no host copy of the whole image. If mapping fails, the file is read instead.
 extern "C" lssm_status lssm_model_load(lssm_ctx* ctx, const char* path, lssm_model** out) {
     if (!ctx || !path || !out) return fail(LSSM_ERR_INVALID_ARGUMENT, "lssm_model_load: null argument");
-    std::ifstream f(path, std::ios::binary | std::ios::ate);
-    if (!f) return fail(LSSM_ERR_INVALID_ARGUMENT, "MmapFile: cannot open '%s'", path);
-    const std::streamsize n = f.tellg();
-    f.seekg(0);
-    std::vector<uint8_t> buf((size_t)n);
-    if (n > 0 && !f.read(reinterpret_cast<char*>(buf.data()), n)) return fail(LSSM_ERR_FORMAT, "cannot read '%s'", path);
-    return lssm_model_load_bytes(ctx, buf.data(), buf.size(), out);
+    const int fd = ::open(path, O_RDONLY);
+    if (fd < 0) return fail(LSSM_ERR_INVALID_ARGUMENT, "MmapFile: cannot open '%s'", path);
+    struct stat st {};
+    if (::fstat(fd, &st) != 0) {
+        ::close(fd);
+        return fail(LSSM_ERR_INVALID_ARGUMENT, "MmapFile: cannot stat '%s'", path);
+    }
+    const size_t n = (size_t)st.st_size;
+    if (n == 0) {
+        ::close(fd);
+        return fail(LSSM_ERR_FORMAT, "MmapFile: empty or invalid file '%s'", path);
+    }
+    void* map = ::mmap(nullptr, n, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (map == MAP_FAILED) {
+        std::vector<uint8_t> buf(n);
+        size_t got = 0;
+        while (got < n) {
+            const ssize_t r = ::read(fd, buf.data() + got, n - got);
+            if (r <= 0) break;
+            got += (size_t)r;
+        }
+        ::close(fd);
+        if (got < n) return fail(LSSM_ERR_FORMAT, "cannot read '%s'", path);
+        return lssm_model_load_bytes(ctx, buf.data(), n, out);
+    }
+    ::close(fd);
+    ::madvise(map, n, MADV_SEQUENTIAL);
+    const lssm_status stt = lssm_model_load_bytes(ctx, map, n, out);
+    ::munmap(map, n);
+    return stt;
 }
 
 // Tensor list of a Mamba2ForCausalLM state_dict, in its order (the order the

@@ -142,6 +142,26 @@ def test_synthesized_batch16_split_gemm_vs_oracle(ctx):
         np.testing.assert_array_less(np.abs(last[b] - ostep[-1]), 0.1 + 4e-3 * np.abs(ostep[-1]))
 
 
+def test_model_file_load_multi_piece(ctx, tmp_path):
+    """A model file several 64 MiB staging pieces long: loaded through the file mapping and the
+    double-buffered pinned upload, its HBM image equals the saved bytes; open / empty-file errors
+    are reported like MmapFile's."""
+    hp = dict(d_model=2560, n_layer=2, d_state=128, d_conv=4, expand=2, vocab_size=50288, n_heads=80, d_head=64,
+              chunk_size=256, n_groups=1, norm_before_gate=0)
+    m = lssm.Model.synthesize(ctx, lssm.hparams(**hp), seed=12, int4=True)
+    path = tmp_path / "synth.ssm"
+    m.save(path)
+    data = path.read_bytes()
+    assert len(data) > 3 * (64 << 20)
+    loaded = lssm.Model.load(ctx, path)
+    assert loaded.download_bytes() == data
+    with pytest.raises(lssm.LssmError, match="cannot open"):
+        lssm.Model.load(ctx, tmp_path / "missing.ssm")
+    (tmp_path / "empty.ssm").write_bytes(b"")
+    with pytest.raises(lssm.LssmError, match="empty or invalid"):
+        lssm.Model.load(ctx, tmp_path / "empty.ssm")
+
+
 def test_engine_errors(ctx, golden):
     model = lssm.Model.load(ctx, golden / "tinyB_fp16.ssm")
     s = lssm.Session(ctx, model, batch=1, max_seq_len=8)
