@@ -218,7 +218,7 @@ lssm_status lssm_ssd_step_batched(lssm_ctx* ctx, const void* x, const void* B, c
                                   const void* dt_bias, const void* A_log, const void* D_skip, void* state_io,
                                   void* y, lssm_ssd_batched_dims dims);
 
-/* ---- engine: .ssm model + session (the callers of the ops: src/model/*.cpp, src/runtime/*.cpp) ---- */
+/* ---- engine: .ssm model + session (the callers of the ops: the .cpp files of src/model and src/runtime) ---- */
 typedef struct lssm_model lssm_model;
 typedef struct lssm_session lssm_session;
 
