@@ -12,9 +12,13 @@
 //     linear.metal:538) and write the fp16 B tile in the 128-byte-swizzled K-major
 //     layout the UMMA descriptor expects;
 //   * warp 1 issues tcgen05.mma (M 128, N BN, K 16) into a double-buffered TMEM
-//     accumulator; warps 2..5 drain TMEM to fp16 (optionally SiLU) in global memory.
+//     accumulator; warps 2..5 drain TMEM to fp16 (SiLU, residual or fp32 epilogues) in
+//     global memory.
 // Scales are read by the dequant threads straight from global memory, 8 blocks
-// (16 bytes) at a time, two loads ahead. Persistent CTAs walk (m, n) tiles.
+// (16 bytes) at a time, two loads ahead. Persistent CTAs walk (m, n, k-split) units:
+// with M <= 128 the launcher may split K (on 256-wide scale groups) so the units fill the
+// SMs; each split then writes fp32 partials and k_splitk_reduce sums them in split order
+// and applies the epilogue.
 // Every wait is bounded (2 s) and reports through the shared tensor-core error word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
