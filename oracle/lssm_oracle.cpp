@@ -468,7 +468,7 @@ void lssm_oracle_ssd_chunked_f16(const uint16_t* X, const uint16_t* Bp, const ui
 }
 
 // ---------------------------------------------------------------------------
-//  SSD, generic precision (the BASELINE SSD-op configuration and the exact check).
+//  SSD, generic precision (the standalone SSD-op benchmark configuration and the exact check).
 //  Same recurrence as ssd_step/ssd_chunked, written as the chunked algorithm
 //  (chunk C) with fp32 or double accumulation and no intermediate rounding.
 //  Inputs are pre-converted to fp32 by the caller (bf16 / fp16 sources).
@@ -634,7 +634,7 @@ struct OracleModelDesc {
     uint32_t lm_head_int4;
     // mode: 0 = faithful (fp16 activations, reference chunk cap 64 and fp16-staged
     //       prefill state), 1 = fp32 (no intermediate fp16 rounding of activations;
-    //       the BASELINE "130M fp32" parity configuration; weights are read as stored).
+    //       the 130M-shape fp32 parity configuration; weights are read as stored).
     uint32_t mode;
 };
 
