@@ -132,6 +132,12 @@ lssm_status lssm_linear_int4_gemv(lssm_ctx* ctx, const void* x, size_t x_off, co
 lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:141-145 */
+/* Introspection (no reference counterpart, no device needed): the launch plan the INT4 GEMM
+ * takes for (M, N, K) on `sms` SMs with `ws_bytes` of scratch (16-byte aligned operands and
+ * K % 256 == 0 assumed). Returns 1 and the N tile / K split count when the fused kernel
+ * takes the shape, 0 when it dequantises and runs the fp16 GEMM instead. */
+int lssm_plan_int4_gemm(uint32_t M, uint32_t N, uint32_t K, int sms, size_t ws_bytes, uint32_t* bn,
+                        uint32_t* splits);
 /* Batched-decode extensions (no MetalOps counterpart): the GEMVs above take one activation
  * row (dims.M == 1, the checks of ops.mm:207-212 and :323-324); these take 1 <= dims.M <= 8 rows
  * (the sequences of one decode step, row-major (M, K) in, (M, N) out) and read the weights once

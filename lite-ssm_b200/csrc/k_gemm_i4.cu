@@ -367,25 +367,18 @@ cudaError_t run_gemm_i4(const void* x, const void* packed, const void* scales, v
     return cudaGetLastError();
 }
 
-}  // namespace
+// Launch plan of the fused INT4 GEMM (host only): the N tile (0 = not taken: the caller
+// dequantises, then runs the fp16 GEMM) and the number of K splits.
+struct GemmI4Plan {
+    int bn;
+    uint32_t splits;
+};
 
-// Fused INT4 GEMM for the small-M (batched decode) shapes where it beats dequantising
-// once: returns cudaErrorNotSupported otherwise, or when the operands do not fit the TMA
-// path (K % 256, 16-byte alignment of x / packed / scales); the caller then falls back
-// to dequantise-then-GEMM. `ws` (`ws_bytes`, 16-byte aligned, may be null) lets M <= 128
-// split K over CTAs; `launches` (may be null) receives the number of kernels launched.
-cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
-                           uint32_t K, int epilogue, cudaStream_t s, float* ws, size_t ws_bytes, int* launches) {
-    if (launches) *launches = 0;
-    if (!M || !N || !K) return cudaSuccess;
-    if (K % 256 || !aligned(x, 16) || !aligned(packed, 16) || !aligned(scales, 16)) return cudaErrorNotSupported;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (M > 512) return cudaErrorNotSupported;
+GemmI4Plan plan_gemm_i4(uint32_t M, uint32_t N, uint32_t K, int sms, size_t ws_bytes) {
+    if (!M || !N || !K || K % 256 || M > 512 || sms < 1) return {0, 1};
     const uint32_t mt = (M + I4_BM - 1) / I4_BM;
     const int cands[3] = {256, 128, 64};
-    if (M <= 128 && ws && aligned(ws, 16)) {
+    if (M <= 128 && ws_bytes) {
         // Decode-size M has few (m, n) tiles, and each walks all of K at ~0.4-0.75 us per
         // 64-wide K block (the 3-, 5- and 6-stage rings of BN 256 / 128 / 64): split K over
         // 256-wide groups so the tiles x splits fill the SMs, fp32 partials in ws, then one
@@ -405,18 +398,13 @@ cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales
             const double cost = waves * ((groups + sp - 1) / sp) * 4 * tblk + (sp > 1 ? 2.0 : 0.0);
             if (cost < best - 1e-9) { best = cost; best_bn = c; best_s = sp; }
         }
-        if (best_s > 1) {
-            if (launches) *launches = 2;
-            if (best_bn == 256) return run_gemm_i4<256>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
-            if (best_bn == 128) return run_gemm_i4<128>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
-            return run_gemm_i4<64>(x, packed, scales, y, M, N, K, epilogue, sms, s, best_s, ws);
-        }
+        if (best_s > 1) return {best_bn, best_s};
     }
     // Each M tile re-dequantises its weights: beyond a few M tiles, dequantising once and
     // running the fp16 GEMM is cheaper (2048 x 10576 x 2560: 148 vs 166 us); and with too
     // few N tiles to fill half the SMs the per-tile K loop is exposed. Both go to the caller's
     // dequantise-then-GEMM path.
-    if ((N + 63) / 64 < (uint32_t)sms / 2) return cudaErrorNotSupported;
+    if ((N + 63) / 64 < (uint32_t)sms / 2) return {0, 1};
     // N tile with the fewest idle SM-slots over the persistent waves (small M: more tiles)
     double best = -1.0;
     int best_bn = 128;
@@ -426,10 +414,39 @@ cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales
         const double eff = (double)M * N / ((double)waves * sms * I4_BM * c);
         if (eff > best + 1e-9) { best = eff; best_bn = c; }
     }
-    if (launches) *launches = 1;
-    if (best_bn == 256) return run_gemm_i4<256>(x, packed, scales, y, M, N, K, epilogue, sms, s);
-    if (best_bn == 128) return run_gemm_i4<128>(x, packed, scales, y, M, N, K, epilogue, sms, s);
-    return run_gemm_i4<64>(x, packed, scales, y, M, N, K, epilogue, sms, s);
+    return {best_bn, 1};
+}
+
+}  // namespace
+
+// Fused INT4 GEMM for the small-M (batched decode) shapes where it beats dequantising
+// once: returns cudaErrorNotSupported otherwise, or when the operands do not fit the TMA
+// path (K % 256, 16-byte alignment of x / packed / scales); the caller then falls back
+// to dequantise-then-GEMM. `ws` (`ws_bytes`, 16-byte aligned, may be null) lets M <= 128
+// split K over CTAs; `launches` (may be null) receives the number of kernels launched.
+cudaError_t launch_gemm_i4(const void* x, const void* packed, const void* scales, void* y, uint32_t M, uint32_t N,
+                           uint32_t K, int epilogue, cudaStream_t s, float* ws, size_t ws_bytes, int* launches) {
+    if (launches) *launches = 0;
+    if (!M || !N || !K) return cudaSuccess;
+    if (K % 256 || !aligned(x, 16) || !aligned(packed, 16) || !aligned(scales, 16)) return cudaErrorNotSupported;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const GemmI4Plan p = plan_gemm_i4(M, N, K, sms, (ws && aligned(ws, 16)) ? ws_bytes : 0);
+    if (!p.bn) return cudaErrorNotSupported;
+    float* const w = p.splits > 1 ? ws : nullptr;
+    if (launches) *launches = p.splits > 1 ? 2 : 1;
+    if (p.bn == 256) return run_gemm_i4<256>(x, packed, scales, y, M, N, K, epilogue, sms, s, p.splits, w);
+    if (p.bn == 128) return run_gemm_i4<128>(x, packed, scales, y, M, N, K, epilogue, sms, s, p.splits, w);
+    return run_gemm_i4<64>(x, packed, scales, y, M, N, K, epilogue, sms, s, p.splits, w);
 }
 
 }  // namespace lssm
+
+extern "C" int lssm_plan_int4_gemm(uint32_t M, uint32_t N, uint32_t K, int sms, size_t ws_bytes, uint32_t* bn,
+                                   uint32_t* splits) {
+    const lssm::GemmI4Plan p = lssm::plan_gemm_i4(M, N, K, sms, ws_bytes);
+    if (bn) *bn = (uint32_t)p.bn;
+    if (splits) *splits = p.splits;
+    return p.bn ? 1 : 0;
+}

@@ -1,0 +1,71 @@
+"""CPU: the launch plan of the fused INT4 GEMM (lssm_plan_int4_gemm, the host function the
+launcher uses), over decode, batched and prefill shapes: which shapes the fused kernel takes,
+the N tile, and the K split at decode-size M, against the plan's invariants and the choices
+measured on B200 for the batched in_proj / out_proj."""
+
+import ctypes as C
+import itertools
+
+import pytest
+
+import lssm
+
+SMS = 148
+
+
+def plan(M, N, K, ws_bytes, sms=SMS):
+    bn, sp = C.c_uint32(), C.c_uint32()
+    fused = lssm.lib().lssm_plan_int4_gemm(M, N, K, sms, ws_bytes, C.byref(bn), C.byref(sp))
+    return fused, bn.value, sp.value
+
+
+def k_ranges(nk, splits):
+    """K-block range of each split: splits on 256-wide groups (four 64-wide K blocks)."""
+    g = nk // 4
+    return [(4 * (s * g // splits), 4 * ((s + 1) * g // splits)) for s in range(splits)]
+
+
+@pytest.mark.parametrize("M,N,K,bn,splits", [
+    (64, 10576, 2560, 256, 3),    # batched in_proj: 42 N tiles x 3 splits = 126 CTAs
+    (64, 2560, 5120, 128, 7),     # batched out_proj: 20 N tiles x 7 splits = 140 CTAs
+    (64, 5120, 5120, 256, 7),
+    (16, 10576, 2560, 256, 3),
+])
+def test_measured_choices(M, N, K, bn, splits):
+    assert plan(M, N, K, 8 * M * N * 4) == (1, bn, splits)
+
+
+def test_without_scratch_no_split():
+    # no workspace: no split; out_proj's 40 N tiles are then too few for the fused kernel
+    assert plan(64, 10576, 2560, 0) == (1, 128, 1)
+    assert plan(64, 2560, 5120, 0)[0] == 0
+
+
+def test_not_taken():
+    assert plan(100, 300, 256, 1 << 30)[0] == 0     # one K group: no split, too few N tiles
+    assert plan(17, 33, 96, 1 << 30)[0] == 0        # K % 256
+    assert plan(513, 10576, 2560, 1 << 30)[0] == 0  # beyond a few M tiles: dequantise once
+    assert plan(2048, 10576, 2560, 1 << 30)[0] == 0
+
+
+@pytest.mark.parametrize("M,N,K", list(itertools.product(
+    [1, 9, 16, 33, 64, 100, 128, 129, 256, 512], [300, 1000, 2560, 4810, 5120, 10576, 50288],
+    [256, 768, 2560, 5120])))
+def test_plan_invariants(M, N, K):
+    for ws in (0, 1 << 20, 8 * M * N * 4):
+        fused, bn, sp = plan(M, N, K, ws)
+        if not fused:
+            assert bn == 0 and sp == 1
+            continue
+        assert bn in (64, 128, 256) and M <= 512 and K % 256 == 0
+        tiles = -(-M // 128) * -(-N // bn)
+        if sp == 1:
+            assert (N + 63) // 64 >= SMS // 2
+            continue
+        assert M <= 128 and ws > 0
+        assert 2 <= sp <= min(8, K // 256)
+        assert sp * M * N * 4 <= ws              # partials fit the scratch
+        assert tiles * sp <= SMS                  # one wave of CTAs
+        r = k_ranges(K // 64, sp)                 # every K block in exactly one split
+        assert r[0][0] == 0 and r[-1][1] == K // 64
+        assert all(a < b for a, b in r) and all(r[i][1] == r[i + 1][0] for i in range(sp - 1))
