@@ -124,20 +124,29 @@ lssm_status lssm_linear_silu_f16_gemm(lssm_ctx* ctx, const void* x, size_t x_off
 lssm_status lssm_linear_int4_gemv(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:135-139 */
-/* The INT4 GEMM uses the context's device scratch. For M <= 128 it holds the split-K fp32
- * partials (8*M*N*4 bytes reserved); when the fused kernel cannot take the shape, it holds the
- * dequantised fp16 weight (N*K*2 bytes). The scratch grows by reallocation, which a graph capture
- * cannot hold: under graph batching, first make one call of the same or a larger shape outside
- * the batch. */
+/* The INT4 GEMM uses the context's device scratch (one block per context, on its device). For
+ * M <= 128 it holds the split-K fp32 partials (8*M*N*4 bytes reserved); when the fused kernel
+ * cannot take the shape, it holds the dequantised fp16 weight (N*K*2 bytes). The scratch grows by
+ * allocating a larger block. Growth is refused inside a captured batch (LSSM_ERR_STATE): under
+ * graph batching, first make one call of the same or a larger shape outside the batch. A block
+ * that the kept graph of lssm_replay_batch may use is freed only when that graph is replaced
+ * or the context destroyed, so replays never touch freed memory. */
 lssm_status lssm_linear_int4_gemm(lssm_ctx* ctx, const void* x, size_t x_off, const void* w,
                                   size_t w_packed_off, const void* w_scl, size_t w_scales_off, void* y,
                                   size_t y_off, lssm_linear_dims dims);                 /* ops.hpp:141-145 */
 /* Introspection (no reference counterpart, no device needed): the launch plan the INT4 GEMM
  * takes for (M, N, K) on `sms` SMs with `ws_bytes` of scratch (16-byte aligned operands and
  * K % 256 == 0 assumed). Returns 1 and the N tile / K split count when the fused kernel
- * takes the shape, 0 when it dequantises and runs the fp16 GEMM instead. */
+ * takes the shape, 0 when it dequantises and runs the fp16 GEMM instead. Splitting K needs
+ * room for the fp32 partials of at least two splits: ws_bytes >= 2*M*N*4; below that the
+ * plan has one split. */
 int lssm_plan_int4_gemm(uint32_t M, uint32_t N, uint32_t K, int sms, size_t ws_bytes, uint32_t* bn,
                         uint32_t* splits);
+/* The work unit of CTA-tile `tile` in a fused INT4 GEMM launch of m_tiles x n_tiles x splits
+ * units over nk 64-wide K blocks, computed by the same function the kernel uses:
+ * out[5] = {m tile, n tile, split, first K block, end K block}. */
+void lssm_int4_gemm_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits, uint32_t nk,
+                         uint32_t* out);
 /* Batched-decode extensions (no MetalOps counterpart): the GEMVs above take one activation
  * row (dims.M == 1, the checks of ops.mm:207-212 and :323-324); these take 1 <= dims.M <= 8 rows
  * (the sequences of one decode step, row-major (M, K) in, (M, N) out) and read the weights once

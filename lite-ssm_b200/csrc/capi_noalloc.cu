@@ -82,7 +82,7 @@ extern "C" lssm_status lssm_inproj_fused_f16_noalloc(lssm_ctx* ctx, const void* 
         return fail(LSSM_ERR_INVALID_ARGUMENT,
                     "inproj_fused_f16_noalloc: L * proj_dim * 4 = %llu bytes exceeds the %u-byte static scratch",
                     (unsigned long long)need, LSSM_NOALLOC_SCRATCH_BYTES);
-    if (d.L == 0) return LSSM_OK;
+    if (d.L == 0) return finish_op(ctx, "inproj_fused_f16_noalloc");
     float* mm = nullptr;
     if (lssm_status st = tile_for_device(ctx->device, &mm)) return st;
     for (uint32_t m0 = 0; m0 < d.L; m0 += 8) {
@@ -95,8 +95,7 @@ extern "C" lssm_status lssm_inproj_fused_f16_noalloc(lssm_ctx* ctx, const void* 
                             bp(ssd_B, b_off), bp(ssd_C, c_off), bp(proj_dt, dt_off), bp(proj_xBC, xBC_off), d.L,
                             d.d_inner, GN, d.n_heads, d.d_conv, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "inproj_fused_f16_noalloc");
-    if (ctx->batch_active) return LSSM_OK;
-    e = cudaStreamSynchronize(ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(e, "inproj_fused_f16_noalloc");
-    return LSSM_OK;
+    // the same completion path as every other op: launch error check, then (outside a
+    // batch) wait for the stream and read the device error word
+    return finish_op(ctx, "inproj_fused_f16_noalloc");
 }

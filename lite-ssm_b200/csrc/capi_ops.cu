@@ -62,26 +62,40 @@ lssm_status finish_op(lssm_ctx* ctx, const char* name) {
     return LSSM_OK;
 }
 
-// Caller-visible scratch for the INT4 GEMM's dequantised weight tile (grows on demand).
-struct ScratchArena {
-    void* ptr = nullptr;
-    size_t size = 0;
-};
-static thread_local ScratchArena g_scratch;
-
+// The context's device scratch (see lssm_ctx::scratch). Growing it never frees a block
+// that a kept graph may replay; growing it inside a graph capture is refused, because the
+// allocation would not be part of the graph and the old block's users would be recorded.
 static lssm_status scratch_reserve(lssm_ctx* ctx, size_t n, void** out) {
-    if (g_scratch.size < n) {
-        if (g_scratch.ptr) {
-            cudaStreamSynchronize(ctx->stream);
-            cudaFree(g_scratch.ptr);
-            g_scratch = {};
+    if (ctx->scratch_size < n) {
+        if (ctx->capturing)
+            return fail(LSSM_ERR_STATE,
+                        "scratch of %zu bytes needed inside a captured batch (have %zu): make one call of this "
+                        "shape outside the batch first",
+                        n, ctx->scratch_size);
+        if (ctx->scratch) {
+            if (ctx->last_graph) {
+                ctx->scratch_retired.push_back(ctx->scratch);
+            } else {
+                cudaStreamSynchronize(ctx->stream);
+                cudaFree(ctx->scratch);
+            }
+            ctx->scratch = nullptr;
+            ctx->scratch_size = 0;
         }
-        cudaError_t e = cudaMalloc(&g_scratch.ptr, n);
-        if (e != cudaSuccess) return cuda_fail(e, "scratch allocation");
-        g_scratch.size = n;
+        cudaError_t e = cudaMalloc(&ctx->scratch, n);
+        if (e != cudaSuccess) { ctx->scratch = nullptr; return cuda_fail(e, "scratch allocation"); }
+        ctx->scratch_size = n;
     }
-    *out = g_scratch.ptr;
+    *out = ctx->scratch;
     return LSSM_OK;
+}
+
+// Frees the scratch blocks only the (now replaced or destroyed) kept graph referred to.
+static void scratch_release_retired(lssm_ctx* ctx) {
+    if (ctx->scratch_retired.empty()) return;
+    cudaStreamSynchronize(ctx->stream);
+    for (void* p : ctx->scratch_retired) cudaFree(p);
+    ctx->scratch_retired.clear();
 }
 
 cudaError_t launch_gemv_int4_ex(const void* x, const void* packed, const void* scales, void* y, uint32_t M,
@@ -147,6 +161,9 @@ lssm_status lssm_ctx_destroy(lssm_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->last_graph) cudaGraphExecDestroy(ctx->last_graph);
+    ctx->last_graph = nullptr;
+    scratch_release_retired(ctx);
+    if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->owns_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return LSSM_OK;
@@ -210,6 +227,7 @@ lssm_status lssm_commit_and_wait(lssm_ctx* ctx) {
         cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
         if (e != cudaSuccess) return cuda_fail(e, "commit_and_wait: end capture");
         if (ctx->last_graph) { cudaGraphExecDestroy(ctx->last_graph); ctx->last_graph = nullptr; }
+        scratch_release_retired(ctx);   // only the replaced graph could still use them
         e = cudaGraphInstantiate(&ctx->last_graph, g, 0);
         cudaGraphDestroy(g);
         if (e != cudaSuccess) { ctx->last_graph = nullptr; return cuda_fail(e, "commit_and_wait: instantiate"); }

@@ -78,7 +78,7 @@ __device__ __forceinline__ uint4 dequant_scaled(uint32_t w, __half2 s2) {
 struct I4Unit {
     uint32_t mb, nb, ks, kb0, kb1;
 };
-__device__ __forceinline__ I4Unit i4_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits,
+__host__ __device__ __forceinline__ I4Unit i4_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits,
                                           uint32_t nk) {
     const uint32_t mn = m_tiles * n_tiles, ks = tile / mn, rem = tile - ks * mn, groups = nk / 4;
     return {rem % m_tiles, rem / m_tiles, ks, 4 * (ks * groups / splits), 4 * ((ks + 1) * groups / splits)};
@@ -449,4 +449,12 @@ extern "C" int lssm_plan_int4_gemm(uint32_t M, uint32_t N, uint32_t K, int sms, 
     if (bn) *bn = (uint32_t)p.bn;
     if (splits) *splits = p.splits;
     return p.bn ? 1 : 0;
+}
+
+// The work unit the kernel assigns to CTA-tile `tile` (same function the device code calls):
+// out = {m tile, n tile, split, first K block, end K block}.
+extern "C" void lssm_int4_gemm_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits, uint32_t nk,
+                                    uint32_t* out) {
+    const lssm::I4Unit u = lssm::i4_unit(tile, m_tiles, n_tiles, splits, nk);
+    out[0] = u.mb; out[1] = u.nb; out[2] = u.ks; out[3] = u.kb0; out[4] = u.kb1;
 }

@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "lssm_cuda.h"
 
@@ -28,6 +29,13 @@ struct lssm_ctx {
     bool capture_batches = false;
     bool capturing = false;
     cudaGraphExec_t last_graph = nullptr;
+    // Device scratch of the ops that need one (INT4 GEMM split-K partials or dequantised
+    // weights, the fused in_proj tile), on this context's device. It grows by allocating
+    // a larger block; a superseded block that `last_graph` may still reference is kept in
+    // `scratch_retired` until that graph is replaced or the context is destroyed.
+    void* scratch = nullptr;
+    size_t scratch_size = 0;
+    std::vector<void*> scratch_retired;
 };
 
 namespace lssm {

@@ -4,7 +4,7 @@ in one cooperative launch) against the CPU oracle and against the per-op graph p
 Criteria (same as the engine tests):
   * greedy ids identical to the oracle run teacher-forced on the kernel's ids, a flip
     excused only where the oracle's top-2 gap is inside the 0.1 logit tolerance
-    (tests/test_ssd_parity.cpp:155-164 of the reference);
+    (tests/test_ssd_parity.cpp:155-164 of the reference), at most one per 64 tokens;
   * last-step logits within 0.1 of the oracle;
   * persistent == per-op graph path (ids, and logits within 2e-2: both keep the same
     fp16 rounding points, only fp32 summation order differs);
@@ -17,15 +17,9 @@ import pytest
 
 import lssm
 import pyoracle as po
+from parity_util import assert_ids
 
 pytestmark = pytest.mark.gpu
-
-
-def near_tie_ok(gpu_toks, ora_toks, ora_logits_rows, tol=0.1):
-    for i, (a, b) in enumerate(zip(gpu_toks, ora_toks)):
-        if a != b and abs(ora_logits_rows[i][a] - ora_logits_rows[i][b]) > tol:
-            return False
-    return True
 
 
 def _hp(d_model=256, n_layer=3, vocab=1000, n_groups=1, d_conv=4):
@@ -49,7 +43,7 @@ def test_persistent_matches_oracle(ctx, cfg):
     assert launches[1] == 1, "persistent decode kernel did not run"
     ora = po.OracleModel(m.download_bytes(), mode=0)
     otoks, opre, ostep = ora.generate(prompt[0], 10, teacher=toks[0])
-    assert near_tie_ok(toks[0], otoks, np.concatenate([opre[None], ostep]))
+    assert_ids(toks[0], otoks, np.concatenate([opre[None], ostep]), f"persistent {cfg}")
     assert np.abs(logits[0] - ostep[8]).max() < 0.1
 
 
@@ -86,7 +80,7 @@ def test_persistent_2p7b_shaped_layers(ctx):
     assert launches[1] == 1
     ora = po.OracleModel(m.download_bytes(), mode=0)
     otoks, opre, ostep = ora.generate(prompt[0], 6, teacher=toks[0])
-    assert near_tie_ok(toks[0], otoks, np.concatenate([opre[None], ostep]))
+    assert_ids(toks[0], otoks, np.concatenate([opre[None], ostep]), "persistent 2.7B widths")
     assert np.abs(logits[0] - ostep[4]).max() < 0.1
 
 

@@ -19,10 +19,23 @@ def plan(M, N, K, ws_bytes, sms=SMS):
     return fused, bn.value, sp.value
 
 
-def k_ranges(nk, splits):
-    """K-block range of each split: splits on 256-wide groups (four 64-wide K blocks)."""
-    g = nk // 4
-    return [(4 * (s * g // splits), 4 * ((s + 1) * g // splits)) for s in range(splits)]
+def unit(tile, m_tiles, n_tiles, splits, nk):
+    out = (C.c_uint32 * 5)()
+    lssm.lib().lssm_int4_gemm_unit(tile, m_tiles, n_tiles, splits, nk, out)
+    return tuple(out)
+
+
+def k_ranges(nk, splits, m_tiles=1, n_tiles=1):
+    """K-block range of each split, from the kernel's own unit function (every (m, n) tile
+    of a split gets the same range)."""
+    mn = m_tiles * n_tiles
+    r = []
+    for s in range(splits):
+        units = [unit(s * mn + t, m_tiles, n_tiles, splits, nk) for t in range(mn)]
+        assert len({u[3:] for u in units}) == 1 and all(u[2] == s for u in units)
+        assert sorted((u[0], u[1]) for u in units) == [(m, n) for m in range(m_tiles) for n in range(n_tiles)]
+        r.append(units[0][3:])
+    return r
 
 
 @pytest.mark.parametrize("M,N,K,bn,splits", [
@@ -66,6 +79,14 @@ def test_plan_invariants(M, N, K):
         assert 2 <= sp <= min(8, K // 256)
         assert sp * M * N * 4 <= ws              # partials fit the scratch
         assert tiles * sp <= SMS                  # one wave of CTAs
-        r = k_ranges(K // 64, sp)                 # every K block in exactly one split
+        r = k_ranges(K // 64, sp, -(-M // 128), -(-N // bn))   # every K block in exactly one split
+        assert all(a % 4 == 0 for a, _ in r)      # splits start on 256-wide scale groups
         assert r[0][0] == 0 and r[-1][1] == K // 64
         assert all(a < b for a, b in r) and all(r[i][1] == r[i + 1][0] for i in range(sp - 1))
+
+
+def test_split_needs_room_for_two_partials():
+    """Splitting K needs ws_bytes >= 2*M*N*4 (the fp32 partials of two splits)."""
+    M, N, K = 64, 10576, 2560
+    assert plan(M, N, K, 2 * M * N * 4)[2] >= 2
+    assert plan(M, N, K, 2 * M * N * 4 - 16)[2] == 1

@@ -203,6 +203,50 @@ def test_linear_int4_gemm(ctx, ops, M, N, K):
     close(get16(by, M * N), po.to_f32(ref), rtol=1e-2, atol=2e-3)
 
 
+def test_int4_gemm_scratch_growth_keeps_replayed_graph_valid():
+    """The INT4 GEMM's scratch belongs to the context. A captured batch keeps using its block
+    after a later, larger call grows the scratch outside the batch (the old block is kept
+    until the graph is replaced), and growth inside a capture is refused with a state error."""
+    c = lssm.Ctx(0)
+    ops = lssm.Ops(c)
+    M, N, K = 16, 512, 1024
+    packed, scales = _int4_weights(N, K)
+    x = h(RNG.standard_normal((M, K)))
+    ref = np.zeros(M * N, np.uint16)
+    po.lib().lssm_oracle_linear_int4(po.ptr(x.view(np.uint16)), po.ptr(packed), po.ptr(scales), po.ptr(ref), M, N, K, 1)
+    bp, bs, bx, by = hb(c, packed), hb(c, scales), hb(c, x), lssm.DeviceBuffer(c, M * N * 2)
+    ops.linear_int4_gemm((bx, 0), (bp, 0), (bs, 0), (by, 0), lssm.LinearDims(M, N, K))   # sizes the scratch
+    c.set_graph_batching(True)
+    c.begin_batch()
+    ops.linear_int4_gemm((bx, 0), (bp, 0), (bs, 0), (by, 0), lssm.LinearDims(M, N, K))
+    c.commit_and_wait()
+    c.set_graph_batching(False)
+    # a larger call outside the batch grows the scratch (split-K partials of 128 x 4096)
+    M2, N2 = 128, 4096
+    p2, s2 = _int4_weights(N2, K)
+    x2 = h(RNG.standard_normal((M2, K)))
+    b2p, b2s, b2x, b2y = hb(c, p2), hb(c, s2), hb(c, x2), lssm.DeviceBuffer(c, M2 * N2 * 2)
+    ops.linear_int4_gemm((b2x, 0), (b2p, 0), (b2s, 0), (b2y, 0), lssm.LinearDims(M2, N2, K))
+    by.zero()
+    c.replay_batch(2)
+    c.begin_batch()
+    c.commit_and_wait()
+    close(get16(by, M * N), po.to_f32(ref), rtol=1e-2, atol=2e-3)
+    # growth inside a capture: refused, and the context stays usable
+    M3, N3 = 128, 8192
+    p3, s3 = _int4_weights(N3, K)
+    b3p, b3s, b3y = hb(c, p3), hb(c, s3), lssm.DeviceBuffer(c, M3 * N3 * 2)
+    c.set_graph_batching(True)
+    c.begin_batch()
+    with pytest.raises(lssm.LssmError, match="inside a captured batch"):
+        ops.linear_int4_gemm((b2x, 0), (b3p, 0), (b3s, 0), (b3y, 0), lssm.LinearDims(M3, N3, K))
+    c.commit_and_wait()
+    c.set_graph_batching(False)
+    ops.linear_int4_gemm((bx, 0), (bp, 0), (bs, 0), (by, 0), lssm.LinearDims(M, N, K))
+    close(get16(by, M * N), po.to_f32(ref), rtol=1e-2, atol=2e-3)
+    c.close()
+
+
 def test_elementwise(ctx, ops):
     n = 10007
     x = h(RNG.standard_normal(n) * 4)

@@ -56,6 +56,36 @@ def test_noalloc_matches_allocating_entry_point():
     ctx.close()
 
 
+def test_noalloc_leaves_device_memory_unchanged():
+    """After the first call on the device (which looks up the array's address and makes
+    the driver load the module that holds it), further calls take no device memory:
+    cudaMemGetInfo's free bytes are the same before and after them. An L == 0 call
+    returns through the same completion checks as the other ops."""
+    import torch
+
+    ctx = lssm.Ctx(0)
+    rng = np.random.default_rng(5)
+    L, dm, di, N, G, H, K = 16, 768, 1536, 128, 1, 24, 4
+    GN, xd = G * N, di + 2 * G * N
+    proj = di + xd + H
+    dims = lssm.FusedInProjDims(L, dm, di, N, G, H, K, proj)
+    ins = [_dev(ctx, a) for a in (rng.standard_normal((L, dm)).astype(np.float16),
+                                  (rng.standard_normal((proj, dm)) / np.sqrt(dm)).astype(np.float16),
+                                  rng.uniform(-0.5, 0.5, (xd, K)).astype(np.float16),
+                                  rng.uniform(-0.5, 0.5, xd).astype(np.float16))]
+    outs = [lssm.DeviceBuffer(ctx, n * 2) for n in (L * di, L * di, L * GN, L * GN, L * H, L * xd)]
+    _call(ctx, "lssm_inproj_fused_f16_noalloc", ins, outs, dims)       # first call: set-up
+    torch.cuda.synchronize(0)
+    free0, _ = torch.cuda.mem_get_info(0)
+    for _ in range(3):
+        _call(ctx, "lssm_inproj_fused_f16_noalloc", ins, outs, dims)
+    _call(ctx, "lssm_inproj_fused_f16_noalloc", ins, outs, lssm.FusedInProjDims(0, dm, di, N, G, H, K, proj))
+    torch.cuda.synchronize(0)
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes across no-allocation calls"
+    ctx.close()
+
+
 def test_noalloc_rejects_requests_beyond_its_scratch():
     ctx = lssm.Ctx(0)
     buf = lssm.DeviceBuffer(ctx, 64)
