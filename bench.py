@@ -263,13 +263,28 @@ def cpu_baseline_sample(seed=0, prompt=32, new=8, hp=None):
     t_dec = max(t_all - t_pre, 1e-9)
     return dict(prefill_tok_s=prompt / t_pre, decode_tok_s=new / t_dec, cores=po.lib().lssm_oracle_num_threads(),
                 sample=f"prompt {prompt} + {new} greedy tokens, full 64-layer 2.7B INT4 model (synth {t_synth:.1f}s)",
-                seconds=t_pre + t_all, prompt=toks, ids=ids, pre_logits=pre_logits, last_logits=step_logits[-1])
+                seconds=t_pre + t_all, prompt=toks, ids=ids, pre_logits=pre_logits, last_logits=step_logits[-1],
+                oracle=m)
 
 
-def parity_vs_oracle(sess, cb, tol=0.1):
-    """The GPU engine on the CPU sample's prompt (same 64-layer model bytes): greedy ids
-    must equal the oracle's free-running ids, and the prefill / last-step logits must be
-    within `tol` of the fp16-faithful oracle's."""
+def oracle_fp32_rows(cb):
+    """The same sample through the oracle's fp32 mode (not timed): prefill and last-step
+    logits, conditioned on the fp16-faithful run's ids."""
+    m = cb["oracle"]
+    m.desc.mode = 1
+    try:
+        _, pre, steps = m.generate(cb["prompt"], len(cb["ids"]), teacher=cb["ids"])
+    finally:
+        m.desc.mode = 0
+    return pre, steps[-1]
+
+
+def parity_vs_oracle(sess, cb):
+    """The GPU engine on the CPU sample's prompt (same 64-layer model bytes): greedy ids must
+    equal the fp16-faithful oracle's free-running ids, and the prefill / last-step logits must
+    be within twice the oracle's own fp16-faithful vs fp32 spread on the same rows (floor 0.1):
+    the engine and the faithful oracle share every fp16 rounding point and differ only in fp32
+    summation order."""
     n = len(cb["ids"])
     sess.reset()
     first = sess.prefill(cb["prompt"][None])
@@ -279,11 +294,16 @@ def parity_vs_oracle(sess, cb, tol=0.1):
     ids = np.concatenate([first, rest])
     diff = np.nonzero(ids != cb["ids"])[0]
     d = int(diff[0]) if len(diff) else n
+    pre32, last32 = oracle_fp32_rows(cb)
+    noise = max(float(np.abs(cb["pre_logits"] - pre32).max()), float(np.abs(cb["last_logits"] - last32).max()))
+    tol = max(0.1, 2.0 * noise)
     e_pre = float(np.abs(pre - cb["pre_logits"]).max())
     e_last = float(np.abs(last - cb["last_logits"]).max()) if d == n else None
-    ok = d == n and e_pre < tol and e_last < tol
+    ok = d == n and e_pre <= tol and e_last <= tol
     return {"ok": bool(ok), "ids_equal": d == n, "tokens": n, "first_divergence": d, "prompt": len(cb["prompt"]),
             "max_abs_logits_prefill": e_pre, "max_abs_logits_last": e_last, "tolerance": tol,
+            "oracle_fp16_vs_fp32_spread": noise, "max_abs_logit": float(np.abs(pre32).max()),
+            "max_abs_logits_vs_fp32": float(max(np.abs(pre - pre32).max(), np.abs(last - last32).max())),
             "oracle": "fp16-faithful C++ oracle, free-running, same synthesized 64-layer 2.7B INT4 model",
             "decode_path": "persistent" if n_dec_launches(sess) == 1 else "per-op graph"}
 

@@ -57,15 +57,18 @@ namespace lssm {
 
 namespace {
 
-// 7 consumer warps + 1 producer warp: with 8 warps each SM sub-partition holds two,
-// so the kernel may use up to 255 registers per thread (a 9th warp caps it at 168).
-constexpr int CONS_WARPS = 7, CONS = CONS_WARPS * 32, THREADS = CONS + 32;
+// 10 consumer warps + 1 producer warp (352 threads, <= 184 registers each). An INT4 ring
+// stage holds 16 rows x 5 segments of 256 k; consumer warp w reads half of segment w / 2
+// (four 32-wide blocks), so the 10 warps split every stage evenly.
+constexpr int CONS_WARPS = 10, CONS = CONS_WARPS * 32, THREADS = CONS + 32;
 constexpr int RING = 11;
 constexpr uint32_t STAGE = 12288;                         // 1024-aligned (128-byte swizzle atoms)
+constexpr uint32_t NOCT = 2;                              // staged octets (or residual quads) per thread
 constexpr uint32_t SEG_MAX = 5;                           // 16 x 5 x 128 B + INT4 scales <= STAGE
 constexpr uint32_t TG = 5;                                // tiles per register-accumulated group
 constexpr uint32_t XBUF = 20480;                          // staged activation (<= 2 x 5120 halves)
-constexpr uint32_t PART = TG * CONS_WARPS * 32 * 4 * 4;   // per-warp partial sums of one group
+constexpr uint32_t PART = TG * CONS_WARPS * 8 * 4 * 4;    // per-warp partial sums of one group ([ti][warp][g][4])
+constexpr uint32_t XSUM = 2 * 5120 / 32 * 4;              // per-block sums of the staged activation (fp32)
 constexpr uint32_t SBUF = 36864;                          // this CTA's ssd state rows (<= 72 x 128 fp32)
 constexpr uint32_t SROWS = SBUF / 512;
 constexpr uint32_t HBUF = 10240;                          // hidden vector(s) (B x d_model fp16)
@@ -74,7 +77,8 @@ constexpr uint32_t NCH_MAX = 4;                           // out_proj K chunks (
 constexpr uint32_t LT_MAX = 64;                           // layers whose table entries fit in smem
 constexpr uint32_t OFF_RING = 0;
 constexpr uint32_t OFF_X = OFF_RING + RING * STAGE;
-constexpr uint32_t OFF_PART = OFF_X + XBUF;
+constexpr uint32_t OFF_XSUM = OFF_X + XBUF;
+constexpr uint32_t OFF_PART = OFF_XSUM + XSUM;
 constexpr uint32_t OFF_S = OFF_PART + PART;
 constexpr uint32_t OFF_H = OFF_S + SBUF;
 constexpr uint32_t OFF_BC = OFF_H + HBUF;                 // BSLOTS x {B, C} x 128 halves
@@ -83,8 +87,8 @@ constexpr uint32_t OFF_RSLOT = OFF_ROWV + SROWS * 6 * 4;  // SROWS slot ids + BS
 constexpr uint32_t OFF_LT = OFF_RSLOT + 128;              // layer table
 constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
-constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[16], tok[2], abort, arg v[16] / i[16]
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 256;
+constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[32], tok[2], abort, slots, arg v[32] / i[32]
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 512;
 constexpr uint64_t SPIN_NS = 2000000000ull;
 static_assert(SMEM_BYTES <= 232448, "persistent decode kernel exceeds 227 KB of shared memory");
 static_assert(sizeof(PLayer) % 8 == 0 && OFF_BAR % 8 == 0, "layer table / barriers misaligned");
@@ -162,51 +166,74 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
     return line * 128 + ((j ^ (line & 7)) << 4);
 }
 
-// INT4 chunk (16 rows x seg*256 k): this warp's share of the chunk's 32-wide blocks.
-// x is staged over the whole K in fragment order (4 uint4 per 32-k block). Rows g and
-// g + 8 share the swizzle phase (8 * seg lines apart), so one offset serves both.
+// INT4 chunk (16 rows x seg*256 k) in column mode: warp w takes half h = w & 1 of
+// segment s = w >> 1 (four 32-wide blocks); warps beyond 2 * seg have no work in the stage.
+// Each of the MMA's 8 columns carries one (block, sequence) pair: with one sequence,
+// column j is block 8s + j (this half uses columns 4h..4h+3); with two, column 2j + m is
+// block 8s + 4h + j of sequence m. Only the lanes of a column's group supply that block's
+// activation fragment (the others zero), so after the four blocks column n holds
+// sum_k W[row][k] x_n[k] of its block alone and the scales are applied once per column.
+// The weights use the bias-folded dequantisation (exact fp16 values 72 + q); the folded
+// 72 * sum(x) of each block is cancelled by starting the accumulator at -72 * xsum.
+// acc: rows g / g + 8 (one sequence: acc[0] / acc[2]; two: acc[0..1] / acc[2..3] per m).
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
-                                             uint32_t K8, uint32_t M, float acc[4]) {
+                                             const float* xsum, uint32_t K8, uint32_t K32, uint32_t M,
+                                             float acc[4]) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t sgi = warp >> 1, h = warp & 1;
+    if (sgi >= seg) return;
     const uint32_t g = lane >> 2, c = lane & 3;
-    const uint32_t nb = seg * 8, rowb = seg * 128;
-    const uint8_t* ra = stage + g * rowb + 4 * c;
-    const uint8_t* rb = ra + 8 * rowb;
-    const uint32_t sw = (g * seg) & 7;
-    const __half* sc = reinterpret_cast<const __half*>(stage + 16 * rowb);
-    const __half* sa = sc + g * nb;
-    const __half* sbp = sa + 8 * nb;
-    const bool has_x = g < M;
-    const uint4* xrow = xs + (uint64_t)(has_x ? g : 0) * K8 + (uint64_t)chunk * nb * 4 + c;
-    const uint32_t b0 = (nb * warp) / CONS_WARPS, b1 = (nb * (warp + 1)) / CONS_WARPS;
-    // Fully unrolled over the warp's (at most MAXB) blocks so their load -> dequant ->
-    // mma chains overlap: at one CTA per SM the GEMV is latency-bound otherwise.
-    constexpr uint32_t MAXB = (SEG_MAX * 8 + CONS_WARPS - 1) / CONS_WARPS;
-    // Predicated rather than exited early: every iteration reads a valid block (past-the-end
-    // ones re-read block b0 with a zero scale), so the loads of all blocks can be issued
-    // ahead of the arithmetic.
+    const uint32_t rowb = seg * 128;
+    const uint32_t line = g * seg + sgi;                 // 128-byte line of row g, segment sgi
+    const uint32_t hp = ((4 * h) ^ (line & 7)) << 4;     // swizzled 16-byte chunk of block 4h (rows g, g + 8)
+    const uint8_t* ra = stage + line * 128 + 4 * c;
+    const uint32_t rb8 = 8 * rowb;
+    const uint32_t blk0 = chunk * seg * 8 + sgi * 8;     // first block of the segment (whole-K index)
+    const __half* sc = reinterpret_cast<const __half*>(stage + 16 * rowb) + g * seg * 8 + sgi * 8;
+    // this lane's column: block (within the half) and sequence
+    const bool one = M == 1;
+    const uint32_t myj = one ? (g & 3) : (g >> 1), mym = one ? 0 : (g & 1);
+    const bool act = one ? ((g >> 2) == h) : true;
+    const uint4 xg = act ? xs[(uint64_t)mym * K8 + (uint64_t)(blk0 + 4 * h + myj) * 4 + c] : make_uint4(0, 0, 0, 0);
+    // accumulator start: -72 * block sum of the lane's two columns (rows g and g + 8 share them)
+    float i0, i1;
+    if (one) {   // columns 2c, 2c + 1 = blocks 2c, 2c + 1 of the segment; live in half c >> 1
+        const bool live = (c >> 1) == h;
+        const float2 xsv = *reinterpret_cast<const float2*>(xsum + blk0 + 2 * c);
+        i0 = live ? -72.0f * xsv.x : 0.0f;
+        i1 = live ? -72.0f * xsv.y : 0.0f;
+    } else {     // columns 2c, 2c + 1 = block 4h + c of sequences 0, 1
+        i0 = -72.0f * xsum[blk0 + 4 * h + c];
+        i1 = -72.0f * xsum[K32 + blk0 + 4 * h + c];
+    }
+    float da[4] = {i0, i1, i0, i1}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (uint32_t i = 0; i < MAXB; ++i) {
-        const bool live = b0 + i < b1;
-        const uint32_t b = live ? b0 + i : b0;
-        const uint32_t s = b >> 3;
-        const uint32_t off = (s << 7) + (((b & 7) ^ ((sw + s) & 7)) << 4);
-        const uint4 xf = has_x ? xrow[b * 4] : make_uint4(0, 0, 0, 0);
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t off = hp ^ (j << 4);
         const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
-        const uint32_t wb = *reinterpret_cast<const uint32_t*>(rb + off);
+        const uint32_t wb = *reinterpret_cast<const uint32_t*>(ra + rb8 + off);
         uint32_t qa[4], qb[4];
-        dequant_word(wa, qa);
-        dequant_word(wb, qb);
-        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        dequant_word_fold(wa, qa);
+        dequant_word_fold(wb, qb);
+        const bool mine = myj == j;
+        const uint32_t bx = mine ? xg.x : 0u, by = mine ? xg.y : 0u, bz = mine ? xg.z : 0u, bw = mine ? xg.w : 0u;
         const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
         const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
-        mma_16816(d, a1, xf.x, xf.y);
-        mma_16816(d, a2, xf.z, xf.w);
-        const float fa = live ? __half2float(sa[b]) : 0.0f, fb = live ? __half2float(sbp[b]) : 0.0f;
-        acc[0] += d[0] * fa;
-        acc[1] += d[1] * fa;
-        acc[2] += d[2] * fb;
-        acc[3] += d[3] * fb;
+        mma_16816(da, a1, bx, by);
+        mma_16816(db, a2, bz, bw);
+    }
+    const float d0 = da[0] + db[0], d1 = da[1] + db[1], d2 = da[2] + db[2], d3 = da[3] + db[3];
+    if (one) {
+        const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(sc + 2 * c));
+        const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(sc + 8 * seg * 8 + 2 * c));
+        acc[0] += d0 * sa.x + d1 * sa.y;
+        acc[2] += d2 * sb.x + d3 * sb.y;
+    } else {
+        const float sa = __half2float(sc[4 * h + c]), sb = __half2float(sc[8 * seg * 8 + 4 * h + c]);
+        acc[0] += d0 * sa;
+        acc[1] += d1 * sa;
+        acc[2] += d2 * sb;
+        acc[3] += d3 * sb;
     }
 }
 
@@ -237,18 +264,54 @@ __device__ __forceinline__ void consume_f16(const uint8_t* stage, uint32_t seg, 
     }
 }
 
-// RMSNorm of M <= 2 rows of `src` (length K, K % 8 == 0, K / 8 <= 3 * CONS) with weight
+// One staged octet q of sequence m: half(x * w * rr) (rmsnorm_f16 arithmetic) -> xbuf, in
+// the INT4 MMA fragment order {x0,x4} {x1,x5} {x2,x6} {x3,x7} when frag; with frag also the
+// fp32 sum of its 32-wide block's staged values -> xsum[m][q / 4] (the four octets of a block
+// belong to four consecutive threads: a quad shuffle). Every consumer thread calls it;
+// `valid` = q < nq (uniform over each quad, as nq % 4 == 0).
+__device__ __forceinline__ void stage_octet(uint4 xv, uint4 wv, float rr, bool frag, bool valid, uint32_t m,
+                                            uint32_t q, uint32_t nq, uint8_t* xbuf, float* xsum) {
+    float s8 = 0.0f;
+    if (valid) {
+        const __half* xh8 = reinterpret_cast<const __half*>(&xv);
+        const __half* wh8 = reinterpret_cast<const __half*>(&wv);
+        __half v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(xh8[j]) * __half2float(wh8[j]) * rr);
+        uint4 u;
+        if (frag) {
+            __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
+            __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
+            u.x = *reinterpret_cast<uint32_t*>(&o0);
+            u.y = *reinterpret_cast<uint32_t*>(&o1);
+            u.z = *reinterpret_cast<uint32_t*>(&o2);
+            u.w = *reinterpret_cast<uint32_t*>(&o3);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s8 += __half2float(v[j]);
+        } else {
+            u = *reinterpret_cast<uint4*>(v);
+        }
+        reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
+    }
+    if (frag) {
+        s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+        s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+        if (valid && (q & 3) == 0) xsum[m * (nq >> 2) + (q >> 2)] = s8;
+    }
+}
+
+// RMSNorm of M <= 2 rows of `src` (length K, K % 8 == 0, K / 8 <= NOCT * CONS) with weight
 // w -> staged fp16 values (rmsnorm_f16 arithmetic, shaders/norm.metal:51-79); `frag`
 // selects the INT4 MMA fragment permutation (quads x[8q + {0,4,1,5,2,6,3,7}]). Each
-// thread owns up to 3 octets of each row, loaded once (with the weights) as 16-byte
+// thread owns up to NOCT octets of each row, loaded once (with the weights) as 16-byte
 // vectors through L2 (other CTAs wrote the rows); both rows' loads are issued before
 // either reduction.
 __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_t* tok, const __half* embed,
-                           const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* red) {
+                           const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* xsum, float* red) {
     const uint32_t tid = threadIdx.x, nq = K / 8;
-    uint4 xv[2][3], wv[3];
+    uint4 xv[2][NOCT], wv[NOCT];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < (int)NOCT; ++i) {
         const uint32_t q = tid + i * CONS;
         if (q < nq) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + q);
     }
@@ -257,7 +320,7 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
         if (m >= M) break;
         const __half* xr = tok ? embed + (uint64_t)tok[m] * K : src + (uint64_t)m * src_stride;
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < (int)NOCT; ++i) {
             const uint32_t q = tid + i * CONS;
             if (q < nq) xv[m][i] = __ldcg(reinterpret_cast<const uint4*>(xr) + q);
         }
@@ -267,7 +330,7 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
         if (m >= M) break;
         float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < (int)NOCT; ++i) {
             if (tid + i * CONS < nq) {
                 const __half2* h2 = reinterpret_cast<const __half2*>(&xv[m][i]);
 #pragma unroll
@@ -278,7 +341,7 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
             }
         }
         ss = warp_sum(ss);
-        if ((tid & 31) == 0) red[m * 8 + (tid >> 5)] = ss;
+        if ((tid & 31) == 0) red[m * 16 + (tid >> 5)] = ss;
     }
     cons_sync();
 #pragma unroll
@@ -286,29 +349,12 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
         if (m >= M) break;
         float tot = 0.0f;
 #pragma unroll
-        for (int i = 0; i < CONS_WARPS; ++i) tot += red[m * 8 + i];
+        for (int i = 0; i < CONS_WARPS; ++i) tot += red[m * 16 + i];
         const float rr = rsqrtf(tot / (float)K + 1e-5f);
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < (int)NOCT; ++i) {
             const uint32_t q = tid + i * CONS;
-            if (q >= nq) continue;
-            const __half* xh8 = reinterpret_cast<const __half*>(&xv[m][i]);
-            const __half* wh8 = reinterpret_cast<const __half*>(&wv[i]);
-            __half v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(xh8[j]) * __half2float(wh8[j]) * rr);
-            uint4 u;
-            if (frag) {
-                __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
-                __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
-                u.x = *reinterpret_cast<uint32_t*>(&o0);
-                u.y = *reinterpret_cast<uint32_t*>(&o1);
-                u.z = *reinterpret_cast<uint32_t*>(&o2);
-                u.w = *reinterpret_cast<uint32_t*>(&o3);
-            } else {
-                u = *reinterpret_cast<uint4*>(v);
-            }
-            reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
+            stage_octet(q < nq ? xv[m][i] : make_uint4(0, 0, 0, 0), wv[i], rr, frag, q < nq, m, q, nq, xbuf, xsum);
         }
     }
     cons_sync();
@@ -320,28 +366,28 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
 // hidden = embed[tok[m]] at layer 0. `hid` (shared memory) keeps the updated vector for
 // the next layer; the normalised fp16 values go to xbuf as in stage_norm. Every SM
 // computes the same vector (same inputs, same order of additions). The residual pass
-// works on 4-element quads (<= 3 per thread: K <= 2688), all slot loads in flight at once.
+// works on 4-element quads (<= NOCT per thread: K <= 2560), all slot loads in flight at once.
 __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* tok, const __half* embed, __half* hid,
-                             const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* red) {
+                             const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* xsum, float* red) {
     const uint32_t tid = threadIdx.x, nq = K / 8, n4 = K / 4;
-    uint4 wv[3];
+    uint4 wv[NOCT];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < (int)NOCT; ++i) {
         const uint32_t q = tid + i * CONS;
         if (q < nq) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + q);
     }
     for (uint32_t m = 0; m < M; ++m) {
         __half* hrow = hid + (uint64_t)m * K;
-        uint2 hv[3];
-        float4 o[3];
+        uint2 hv[NOCT];
+        float4 o[NOCT];
         // slots summed two at a time (c = 0, 1 then 2, 3): the same fixed order, and at
         // most 6 float4 loads in flight per thread
 #pragma unroll
         for (uint32_t c0 = 0; c0 < NCH_MAX; c0 += 2) {
             if (tok || c0 >= nch) break;
-            float4 pa[3][2];
+            float4 pa[NOCT][2];
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {
+            for (int i = 0; i < (int)NOCT; ++i) {
                 const uint32_t q = tid + i * CONS;
                 if (q >= n4) continue;
 #pragma unroll
@@ -350,7 +396,7 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
                         pa[i][c] = __ldcg(reinterpret_cast<const float4*>(opart + ((uint64_t)(c0 + c) * M + m) * K) + q);
             }
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {
+            for (int i = 0; i < (int)NOCT; ++i) {
                 const uint32_t q = tid + i * CONS;
                 if (q >= n4) continue;
 #pragma unroll
@@ -363,7 +409,7 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
         }
         float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < (int)NOCT; ++i) {
             const uint32_t q = tid + i * CONS;
             if (q >= n4) continue;
             hv[i] = tok ? __ldcg(reinterpret_cast<const uint2*>(embed + (uint64_t)tok[m] * K) + q)
@@ -390,27 +436,10 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
         for (int i = 0; i < CONS_WARPS; ++i) tot += red[i];
         const float rr = rsqrtf(tot / (float)K + 1e-5f);
 #pragma unroll
-        for (int i = 0; i < 3; ++i) {
+        for (int i = 0; i < (int)NOCT; ++i) {
             const uint32_t q = tid + i * CONS;
-            if (q >= nq) continue;
-            const uint4 xv = reinterpret_cast<const uint4*>(hrow)[q];
-            const __half* xh8 = reinterpret_cast<const __half*>(&xv);
-            const __half* wh8 = reinterpret_cast<const __half*>(&wv[i]);
-            __half v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(xh8[j]) * __half2float(wh8[j]) * rr);
-            uint4 u;
-            if (frag) {
-                __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
-                __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
-                u.x = *reinterpret_cast<uint32_t*>(&o0);
-                u.y = *reinterpret_cast<uint32_t*>(&o1);
-                u.z = *reinterpret_cast<uint32_t*>(&o2);
-                u.w = *reinterpret_cast<uint32_t*>(&o3);
-            } else {
-                u = *reinterpret_cast<uint4*>(v);
-            }
-            reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
+            const uint4 xv = q < nq ? reinterpret_cast<const uint4*>(hrow)[q] : make_uint4(0, 0, 0, 0);
+            stage_octet(xv, wv[i], rr, frag, q < nq, m, q, nq, xbuf, xsum);
         }
         cons_sync();
     }
@@ -431,20 +460,21 @@ __device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
+__global__ void __maxnreg__(184) k_decode_persist(PParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + RING;
     uint64_t* sfull = empty + RING;       // ssd state rows landed
     uint64_t* sempty = sfull + 1;         // ssd state buffer released by the consumers
-    float* red = reinterpret_cast<float*>(smem + OFF_MISC);              // 2 x 8 floats
-    uint32_t* tok = reinterpret_cast<uint32_t*>(red + 16);                 // 2 tokens
+    float* red = reinterpret_cast<float*>(smem + OFF_MISC);              // 2 x 16 floats
+    uint32_t* tok = reinterpret_cast<uint32_t*>(red + 32);                 // 2 tokens
     volatile int* abort = reinterpret_cast<volatile int*>(tok + 2);
     uint32_t* nslot_s = reinterpret_cast<uint32_t*>(tok + 3);
-    float* argv = reinterpret_cast<float*>(smem + OFF_MISC + 128);         // 16 floats
-    uint32_t* argi = reinterpret_cast<uint32_t*>(argv + 16);              // 16 ids
+    float* argv = reinterpret_cast<float*>(smem + OFF_MISC + 256);         // 32 floats
+    uint32_t* argi = reinterpret_cast<uint32_t*>(argv + 32);              // 32 ids
     PLayer* LT = reinterpret_cast<PLayer*>(smem + OFF_LT);
     float* part = reinterpret_cast<float*>(smem + OFF_PART);
+    float* xsum = reinterpret_cast<float*>(smem + OFF_XSUM);
     uint8_t* xbuf = smem + OFF_X;
     const float* sstate = reinterpret_cast<const float*>(smem + OFF_S);
     __half* hid = reinterpret_cast<__half*>(smem + OFF_H);
@@ -472,10 +502,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     if (p.dconv > 4 || p.dconv < 1 || p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
         (srows + G - 1) / G > SROWS ||
         p.n_layer > LT_MAX || (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || (uint64_t)p.B * p.dm * 2 > HBUF ||
-        p.dm / 8 > 3 * CONS || p.di / 8 > 3 * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
+        p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
         nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
-        p.H % p.G || ((nA + G - 1) / G) * 16 * p.B > CONS || p.dm / 4 > 3 * CONS) {
+        p.H % p.G || ((nA + G - 1) / G) * 16 * p.B > CONS || p.dm / 4 > NOCT * CONS) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -612,7 +642,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) return false;
                     if (p.trace && tid == 0) wait_ns += gtimer() - w0;
                     const uint8_t* stage = smem + OFF_RING + slot * STAGE;
-                    if (int4) consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), K / 8, p.B, acc[ti]);
+                    if (int4)
+                        consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32, p.B,
+                                     acc[ti]);
                     else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, p.B, acc[ti]);
                     __syncwarp();
                     if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
@@ -620,21 +652,33 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 }
             }
         }
+        // per-warp results of rows g / g + 8 -> part[ti][warp][g] = {(g, m0), (g, m1), (g+8, m0), (g+8, m1)}:
+        // INT4 columns are (block, sequence) pairs, summed over the quad's lanes; fp16 (lm_head)
+        // columns are the sequences themselves, held by the quad's lane c = 0
 #pragma unroll
-        for (uint32_t ti = 0; ti < TG; ++ti)
-            if (ti < nt)
-                *reinterpret_cast<float4*>(part + ((ti * CONS_WARPS + warp) * 32 + lane) * 4) =
-                    make_float4(acc[ti][0], acc[ti][1], acc[ti][2], acc[ti][3]);
+        for (uint32_t ti = 0; ti < TG; ++ti) {
+            if (ti >= nt) continue;
+            float v[4] = {acc[ti][0], acc[ti][1], acc[ti][2], acc[ti][3]};
+            if (int4) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v[q] += __shfl_xor_sync(0xffffffffu, v[q], 1);
+                    v[q] += __shfl_xor_sync(0xffffffffu, v[q], 2);
+                }
+            }
+            if ((lane & 3) == 0)
+                *reinterpret_cast<float4*>(part + ((ti * CONS_WARPS + warp) * 8 + (lane >> 2)) * 4) =
+                    make_float4(v[0], v[1], v[2], v[3]);
+        }
         cons_sync();
         return true;
     };
-    // Cross-warp sum of output (unit ordinal ti within the group, row, m): the m16n8
-    // accumulator of lane (g, c) holds rows g / g + 8 and columns (sequences) 2c, 2c + 1.
+    // Cross-warp sum of output (unit ordinal ti within the group, row, sequence m).
     auto reduce_item = [&](uint32_t ti, uint32_t row, uint32_t m) -> float {
-        const uint32_t src = (row & 7) * 4 + (m >> 1), idx = (m & 1) + ((row >> 3) << 1);
+        const uint32_t idx = ((row >> 3) << 1) + m;
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < CONS_WARPS; ++w) s += part[((ti * CONS_WARPS + w) * 32 + src) * 4 + idx];
+        for (int w = 0; w < CONS_WARPS; ++w) s += part[((ti * CONS_WARPS + w) * 8 + (row & 7)) * 4 + idx];
         return s;
     };
     // All units of a split-K GEMV phase: groups of TG units -> partial-sum slots
@@ -685,7 +729,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             }
             // ---- A: residual + RMSNorm, in_proj tiles (all K chunks of a tile), epilogue:
             // z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
-            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.B, p.dm, true, xbuf, red);
+            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.B, p.dm, true, xbuf, xsum,
+                         red);
             stamp(lb + 1);
             for (uint32_t g0 = 0; g0 < ntA && ok; g0 += TG) {
                 const uint32_t nt = min(TG, ntA - g0);
@@ -799,7 +844,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             if (tid == 0) mbar_arrive1(smem_u32(sempty));   // all reads of the state buffer are done
             stamp(lb + 5);
             // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
-            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, p.B, p.di, true, xbuf, red);
+            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, p.B, p.di, true, xbuf, xsum, red);
             stamp(lb + 6);
             if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
@@ -809,7 +854,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         if (!ok) break;
         // ---- residual + norm_f + lm_head + first-max argmax partials
         wait_ns = 0;
-        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.B, p.dm, false, xbuf, red);
+        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.B, p.dm, false, xbuf, xsum, red);
         stamp(lmb + 0);
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
@@ -942,12 +987,12 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     if (sh.H > 65535) return "more than 65535 heads";
     if (sh.dconv < 1 || sh.dconv > 4) return "d_conv must be 1..4";
     if (sh.dm % 256 || sh.di % 256) return "d_model and d_inner must be multiples of 256";
-    if (sh.dm / 8 > 3 * CONS || sh.di / 8 > 3 * CONS) return "d_model / d_inner too wide for the staged RMSNorm";
+    if (sh.dm / 8 > NOCT * CONS || sh.di / 8 > NOCT * CONS) return "d_model / d_inner too wide for the staged RMSNorm";
     if ((uint64_t)sh.B * (sh.dm > sh.di ? sh.dm : sh.di) * 2 > XBUF) return "staged activations exceed 20 KB";
     if (sh.n_layer > LT_MAX) return "more than 64 layers";
     if ((uint64_t)sh.B * sh.dm * 2 > HBUF) return "hidden vectors exceed 10 KB";
     if (((sh.proj + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many in_proj rows per SM";
-    if (sh.dm / 4 > 3 * CONS) return "d_model too wide for the residual pass (<= 2688)";
+    if (sh.dm / 4 > NOCT * CONS) return "d_model too wide for the residual pass (<= 2560)";
     if (sh.H % sh.G) return "n_heads not divisible by n_groups";
     if (((uint64_t)sh.B * sh.H * sh.P + G - 1) / G > SROWS) return "ssd state rows per SM exceed 36 KB";
     *seg_in = odd_seg(sh.dm / 256);
