@@ -57,7 +57,8 @@ namespace lssm {
 
 namespace {
 
-// 10 consumer warps + 1 producer warp (352 threads, <= 184 registers each). An INT4 ring
+// 10 consumer warps + 1 producer warp (352 threads). With 3 warps on some SM sub-partitions
+// (16384 registers each) a thread may use at most 168 registers. An INT4 ring
 // stage holds 16 rows x 5 segments of 256 k; consumer warp w reads half of segment w / 2
 // (four 32-wide blocks), so the 10 warps split every stage evenly.
 constexpr int CONS_WARPS = 10, CONS = CONS_WARPS * 32, THREADS = CONS + 32;
@@ -460,7 +461,10 @@ __device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
 
 }  // namespace
 
-__global__ void __maxnreg__(184) k_decode_persist(PParams p) {
+// NB = sequences (1 or 2), a template parameter so that the one-sequence kernel keeps only
+// the accumulators it uses (11 warps allow 168 registers per thread).
+template <uint32_t NB>
+__global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + RING;
@@ -492,20 +496,20 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
     const uint32_t ntA = cta < nA ? (nA - 1 - cta) / G + 1 : 0;    // this CTA's in_proj tiles
     const uint32_t nuC = cta < uC ? (uC - 1 - cta) / G + 1 : 0;    // this CTA's out_proj units
     const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;    // lm_head tiles
-    const uint32_t srows = p.B * p.H * p.P;
+    const uint32_t srows = NB * p.H * p.P;
     const uint32_t r0 = (uint32_t)(((uint64_t)srows * cta) / G), r1 = (uint32_t)(((uint64_t)srows * (cta + 1)) / G);
     const uint32_t nrows = r1 - r0;
     const uint32_t GN = p.G * p.N, hpg = p.H / p.G;
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
-    if (p.dconv > 4 || p.dconv < 1 || p.B > 2 || p.B < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
+    if (p.dconv > 4 || p.dconv < 1 || NB > 2 || NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
         (srows + G - 1) / G > SROWS ||
-        p.n_layer > LT_MAX || (uint64_t)p.B * max(p.dm, p.di) * 2 > XBUF || (uint64_t)p.B * p.dm * 2 > HBUF ||
+        p.n_layer > LT_MAX || (uint64_t)NB * max(p.dm, p.di) * 2 > XBUF || (uint64_t)NB * p.dm * 2 > HBUF ||
         p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
         nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
-        p.H % p.G || ((nA + G - 1) / G) * 16 * p.B > CONS || p.dm / 4 > NOCT * CONS) {
+        p.H % p.G || ((nA + G - 1) / G) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -536,7 +540,7 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
         *nslot_s = ns;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (tid < p.B) tok[tid] = p.cur[tid];
+    if (tid < NB) tok[tid] = p.cur[tid];
     for (uint32_t i = tid; i < p.n_layer * (uint32_t)(sizeof(PLayer) / 8); i += THREADS)
         reinterpret_cast<uint64_t*>(LT)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
     __syncthreads();
@@ -643,9 +647,9 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
                     if (p.trace && tid == 0) wait_ns += gtimer() - w0;
                     const uint8_t* stage = smem + OFF_RING + slot * STAGE;
                     if (int4)
-                        consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32, p.B,
+                        consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32, NB,
                                      acc[ti]);
-                    else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, p.B, acc[ti]);
+                    else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, NB, acc[ti]);
                     __syncwarp();
                     if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
                     if (++slot == RING) { slot = 0; phase ^= 1; }
@@ -687,17 +691,17 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
         for (uint32_t i0 = 0; i0 < nu; i0 += TG) {
             const uint32_t nt = min(TG, nu - i0);
             if (!consume_group(true, seg, nch, K, true, i0, nt)) return false;
-            if (tid < nt * 16 * p.B) {
-                const uint32_t ti = tid / (16 * p.B), row = (tid / p.B) % 16, m = tid % p.B;
+            if (tid < nt * 16 * NB) {
+                const uint32_t ti = tid / (16 * NB), row = (tid / NB) % 16, m = tid % NB;
                 const uint32_t u = cta + (i0 + ti) * G, r = (u / nch) * 16 + row;
-                if (r < N) slots[((uint64_t)(u % nch) * p.B + m) * N + r] = reduce_item(ti, row, m);
+                if (r < N) slots[((uint64_t)(u % nch) * NB + m) * N + r] = reduce_item(ti, row, m);
             }
             cons_sync();   // partial sums reused by the next group
         }
         return true;
     };
     // Each thread owns one (tile ordinal, row, seq) output of in_proj for the epilogue.
-    const uint32_t tiA = tid / (16 * p.B), rowA = (tid / p.B) % 16, mA = tid % p.B;
+    const uint32_t tiA = tid / (16 * NB), rowA = (tid / NB) % 16, mA = tid % NB;
     const bool ownA = tiA < ntA;
     const uint32_t rA = (cta + tiA * G) * 16 + rowA;           // in_proj output row
     const bool convA = ownA && rA >= p.di && rA < p.di + p.xd;
@@ -729,7 +733,7 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
             }
             // ---- A: residual + RMSNorm, in_proj tiles (all K chunks of a tile), epilogue:
             // z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
-            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.B, p.dm, true, xbuf, xsum,
+            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, NB, p.dm, true, xbuf, xsum,
                          red);
             stamp(lb + 1);
             for (uint32_t g0 = 0; g0 < ntA && ok; g0 += TG) {
@@ -844,7 +848,7 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
             if (tid == 0) mbar_arrive1(smem_u32(sempty));   // all reads of the state buffer are done
             stamp(lb + 5);
             // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
-            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, p.B, p.di, true, xbuf, xsum, red);
+            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, NB, p.di, true, xbuf, xsum, red);
             stamp(lb + 6);
             if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
@@ -854,15 +858,15 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
         if (!ok) break;
         // ---- residual + norm_f + lm_head + first-max argmax partials
         wait_ns = 0;
-        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.B, p.dm, false, xbuf, xsum, red);
+        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, NB, p.dm, false, xbuf, xsum, red);
         stamp(lmb + 0);
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
         for (uint32_t g0 = 0; g0 < ntL && ok; g0 += TG) {
             const uint32_t nt = min(TG, ntL - g0);
             if (!consume_group(false, p.seg_lm, nchL, p.dm, false, g0, nt)) { ok = false; break; }
-            if (tid < nt * 16 * p.B) {
-                const uint32_t ti = tid / (16 * p.B), row = (tid / p.B) % 16, m = tid % p.B;
+            if (tid < nt * 16 * NB) {
+                const uint32_t ti = tid / (16 * NB), row = (tid / NB) % 16, m = tid % NB;
                 const uint32_t r = (cta + (g0 + ti) * G) * 16 + row;
                 if (r < p.V) {
                     const __half vh = __float2half_rn(reduce_item(ti, row, m));
@@ -876,15 +880,15 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
         if (!ok) break;
         if (tr) p.trace[tbase + lmb + 4] = wait_ns;
         // CTA first-max per sequence (thread tid serves sequence tid % B)
-        warp_argmax(bv, bi, p.B);
-        if (lane < p.B) { argv[warp * 2 + lane] = bv; argi[warp * 2 + lane] = bi; }
+        warp_argmax(bv, bi, NB);
+        if (lane < NB) { argv[warp * 2 + lane] = bv; argi[warp * 2 + lane] = bi; }
         cons_sync();
-        if (tid < p.B) {
+        if (tid < NB) {
             float v = -INFINITY;
             uint32_t ix = 0xFFFFFFFFu;
             for (uint32_t w = 0; w < CONS_WARPS; ++w) argmax_take(v, ix, argv[w * 2 + tid], argi[w * 2 + tid]);
-            p.part_val[(uint64_t)cta * p.B + tid] = v;
-            p.part_idx[(uint64_t)cta * p.B + tid] = ix;
+            p.part_val[(uint64_t)cta * NB + tid] = v;
+            p.part_idx[(uint64_t)cta * NB + tid] = ix;
         }
         stamp(lmb + 1);
         if (!grid_sync(p, gen, abort)) { ok = false; break; }
@@ -893,12 +897,12 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
             // all CTAs' partials in one parallel round of loads (entry e serves sequence e % B)
             float v = -INFINITY;
             uint32_t ix = 0xFFFFFFFFu;
-            for (uint32_t e = tid; e < G * p.B; e += CONS)
+            for (uint32_t e = tid; e < G * NB; e += CONS)
                 argmax_take(v, ix, __ldcg(p.part_val + e), __ldcg(p.part_idx + e));
-            warp_argmax(v, ix, p.B);
-            if (lane < p.B) { argv[warp * 2 + lane] = v; argi[warp * 2 + lane] = ix; }
+            warp_argmax(v, ix, NB);
+            if (lane < NB) { argv[warp * 2 + lane] = v; argi[warp * 2 + lane] = ix; }
             cons_sync();
-            if (tid < p.B) {
+            if (tid < NB) {
                 const uint32_t m = tid;
                 float bv2 = -INFINITY;
                 uint32_t bi2 = 0xFFFFFFFFu;
@@ -925,15 +929,17 @@ __global__ void __maxnreg__(184) k_decode_persist(PParams p) {
 // Host launcher: cooperative launch with one CTA per SM (co-residency guaranteed or
 // the launch fails, so the grid barriers cannot wait on a CTA that never runs).
 cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (prm.B < 1 || prm.B > 2) return cudaErrorInvalidValue;
+    const void* fn = prm.B == 1 ? (const void*)k_decode_persist<1> : (const void*)k_decode_persist<2>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persist, THREADS, SMEM_BYTES);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, THREADS, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorNotSupported;
     PParams p = prm;
     void* args[] = {&p};
-    return cudaLaunchCooperativeKernel((void*)k_decode_persist, dim3(sm_count), dim3(THREADS), args, SMEM_BYTES, s);
+    return cudaLaunchCooperativeKernel(fn, dim3(sm_count), dim3(THREADS), args, SMEM_BYTES, s);
 }
 
 // ---------------------------------------------------------------------------
