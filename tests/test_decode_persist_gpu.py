@@ -6,8 +6,8 @@ Criteria (same as the engine tests):
     excused only where the oracle's top-2 gap is inside the 0.1 logit tolerance
     (tests/test_ssd_parity.cpp:155-164 of the reference), at most one per 64 tokens;
   * last-step logits within 0.1 of the oracle;
-  * persistent == per-op graph path (ids, and logits within 2e-2: both keep the same
-    fp16 rounding points, only fp32 summation order differs);
+  * persistent == per-op graph path (ids, and logits within 2e-2 + 2e-3 |logit|: both keep
+    the same fp16 rounding points, only fp32 summation order differs);
   * batch 2 == two batch-1 runs, and the kernel is really the one that ran
     (one decode launch per call).
 """
@@ -55,7 +55,9 @@ def test_persistent_matches_graph_path(ctx):
     tg, lg, lb = _run(ctx, m, prompt, 48, False)
     assert la[1] == 1 and lb[1] > 1
     assert np.array_equal(tp, tg)
-    assert np.abs(lp - lg).max() < 2e-2
+    # 48 decode steps: the column-mode INT4 GEMV sums in another order (and cancels its folded
+    # bias), so single fp16 roundings of the recurrent state differ; a few fp16 ulps of |logit|
+    np.testing.assert_array_less(np.abs(lp - lg), 2e-2 + 2e-3 * np.abs(lg))
 
 
 def test_persistent_batch2_matches_single(ctx):
