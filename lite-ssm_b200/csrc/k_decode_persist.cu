@@ -768,6 +768,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 cons_sync();   // partial sums reused by the next group
             }
             stamp(lb + 2);
+            if (tr) p.trace[tbase + lb + 9] = wait_ns;   // warp 0's ring wait during in_proj
             if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
             stamp(lb + 3);
             // ---- B: ssd_step + gate over this CTA's state rows: B / C vectors of its
@@ -852,7 +853,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             stamp(lb + 6);
             if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
-            if (tr) p.trace[tbase + lb + 9] = wait_ns;
+
             if (!grid_sync(p, gen, abort)) { ok = false; break; }
         }
         if (!ok) break;
