@@ -334,7 +334,8 @@ lssm_status lssm_p2p_wait_selftest(lssm_ctx* ctx, uint64_t spin_ns);
 
 /* Phase trace of the last persistent decode: sm_count x (n_layer * 10 + 6) u64 words.
  * Per layer: [0] layer start, [1] in_proj RMSNorm staged, [2] in_proj + conv done,
- * [3] after grid barrier, [4] ssd_step done, [5] after grid barrier, [6] out_proj RMSNorm
+ * [3] ssd inputs ready (the B / C / dt rows other SMs publish), [4] ssd_step done, [5] after
+ * grid barrier, [6] out_proj RMSNorm
  * staged, [7] out_proj done, [8] producer's first in_proj copy issued, [9] ns the CTA's
  * first consumer warp waited on its weight ring during in_proj. Then lm_head: [0] norm staged, [1] logits +
  * partial argmax done, [2] after grid barrier, [3] token chosen, [4] ns waited on the

@@ -553,6 +553,11 @@ struct lssm_session {
     uint32_t seg_in = 0, seg_out = 0, seg_lm = 0;
     void* d_maps = nullptr;        // CUtensorMap[4 * n_layer + 1]
     float* d_opart = nullptr;      // out_proj partial-sum slots of the persistent kernel
+    // persistent kernel's exchange words between SMs ({payload, epoch} u64; see PParams) and the
+    // epoch of the next launch (every launch uses epochs never used before on these words)
+    uint64_t* d_mb = nullptr;
+    size_t mb_words = 0;
+    uint32_t epoch_next = 1;
     const char* persist_why = "";  // why the persistent kernel is not used ("" = it is)
     uint64_t* d_trace = nullptr;   // phase stamps of the persistent kernel's first step
     bool trace_on = false;
@@ -586,7 +591,7 @@ extern "C" lssm_status lssm_session_destroy(lssm_session* s) {
     if (s->graph) cudaGraphExecDestroy(s->graph);
     void* ps[] = {s->conv, s->ssd, s->hidden, s->normed, s->proj, s->xs, s->Bs, s->Cs, s->ys, s->gated, s->mixn,
                   s->logits, s->lastrows, s->wscratch, s->d_tokens, s->d_cur, s->d_hist, s->d_step, s->d_err,
-                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart,
+                  s->d_players, s->d_part_val, s->d_part_idx, s->d_bar, s->d_trace, s->d_maps, s->d_opart, s->d_mb,
                   s->d_shard, s->d_sumsq, s->d_part32, s->d_gather, s->d_cpair, s->d_pair, s->d_ticket};
     for (void* p : ps)
         if (p) cudaFree(p);
@@ -656,6 +661,11 @@ static lssm_status setup_persistent(lssm_session* s) {
     const size_t nchC = m->d_inner / (s->seg_out * 256);
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_opart), nchC * s->batch * h.d_model * 4, "session: out_proj slots")))
         return st;
+    // exchange words of the in_proj outputs [B][proj]
+    s->mb_words = (size_t)s->batch * m->proj;
+    if ((st = s_alloc(reinterpret_cast<void**>(&s->d_mb), s->mb_words * 8, "session: exchange words"))) return st;
+    if (cudaMemset(s->d_mb, 0, s->mb_words * 8) != cudaSuccess) return fail(LSSM_ERR_CUDA, "session: exchange words");
+    s->epoch_next = 1;
     const size_t parts = (size_t)s->ctx->sm_count * s->batch;
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_val), parts * 4, "session: argmax partials"))) return st;
     if ((st = s_alloc(reinterpret_cast<void**>(&s->d_part_idx), parts * 4, "session: argmax partials"))) return st;
@@ -677,8 +687,11 @@ static PParams persist_params(lssm_session* s, uint32_t n_steps) {
     p.embed = hp(m->embed);
     p.norm_f = hp(m->norm_f);
     p.lm_head = hp(m->lm_head);
-    p.projb = s->proj; p.xs = s->xs; p.Bs = s->Bs; p.Cs = s->Cs; p.opart = s->d_opart;
-    p.gated = s->gated; p.logits = s->logits;
+    p.mb_in = s->d_mb;
+    p.epoch0 = s->epoch_next;
+    p.opart = s->d_opart;
+    p.gated = s->gated;
+    p.logits = s->logits;
     p.part_val = s->d_part_val; p.part_idx = s->d_part_idx;
     p.cur = s->d_cur; p.history = s->d_hist; p.hist_stride = s->hist_cap; p.n_steps = n_steps;
     p.bar = s->d_bar; p.err = tc_error_word();
@@ -1212,7 +1225,16 @@ extern "C" lssm_status lssm_decode(lssm_session* s, const uint32_t* first, uint3
             if (first[b] >= h.vocab_size)
                 return fail(LSSM_ERR_INVALID_ARGUMENT, "Mamba2Model::embed: token_id out of range (decode)");
         CU(cudaMemsetAsync(s->d_bar, 0, 4, st));
+        // epochs [epoch_next, epoch_next + n_steps * n_layer) tag this launch's exchange words;
+        // before the 32-bit tag would wrap, the words are cleared and the count restarts at 1
+        const uint64_t span = (uint64_t)n_steps * h.n_layer;
+        if ((uint64_t)s->epoch_next + span >= 0xFFFFFFF0ull) {
+            if (span >= 0xFFFFFFF0ull) return fail(LSSM_ERR_INVALID_ARGUMENT, "decode: too many steps for one launch");
+            CU(cudaMemsetAsync(s->d_mb, 0, s->mb_words * 8, st));
+            s->epoch_next = 1;
+        }
         PParams pp = persist_params(s, n_steps);
+        s->epoch_next += (uint32_t)span;
         CU(cudaEventRecord(s->ev[2], st));
         CU(launch_decode_persist(pp, s->ctx->sm_count, st));
         CU(cudaEventRecord(s->ev[3], st));

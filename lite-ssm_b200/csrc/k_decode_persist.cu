@@ -15,19 +15,21 @@
 //     ssd state into a separate buffer. Weights do not depend on activations, so it
 //     runs ahead across phase boundaries and grid barriers: HBM stays busy while the
 //     consumers synchronise.
-//   * warps 0..6 consume. Each warp releases a ring slot as soon as it has read it;
+//   * warps 0..9 consume. Each warp releases a ring slot as soon as it has read it;
 //     tiles / units are accumulated in registers in groups of up to 5 and reduced
 //     across warps once per group. Per layer:
 //       A  residual (hidden += half(sum of out_proj slots); every SM keeps the whole
 //          hidden vector in shared memory) + RMSNorm, staged in MMA-fragment order;
-//          in_proj INT4 GEMV tiles (16 rows x all of K) on register-operand mma.sync
-//          (the dequantisation of k_gemv.cu); epilogue: z / dt stored, xBC rows ->
-//          conv-state roll + conv + SiLU -> x, B, C (each epilogue thread loaded its
-//          conv weights / state at layer start)
-//       -- grid barrier --
-//       B  ssd_step + gate on the SM's state rows (already in shared memory), with the
-//          B / C vectors and per-row scalars staged in one parallel round of loads:
-//          S = e^{A dt} S + dt B x, y = C.S + D x, gated = half(silu(z) * half(y))
+//          in_proj INT4 GEMV tiles (16 rows x all of K) on register-operand mma.sync in
+//          column mode (each MMA column one 32-wide block); the SM owns whole channel
+//          units (8 z rows + 8 x rows per tile), so the x / z of its ssd rows stay in
+//          shared memory; the B / C / dt tiles run first on the SMs with fewer units and
+//          are published as {value, epoch} exchange words. Epilogue: xBC rows ->
+//          conv-state roll + conv + SiLU.
+//       -- no grid barrier: B / C / dt are polled from the exchange words --
+//       B  ssd_step + gate on the SM's state rows (already in shared memory):
+//          S = e^{A dt} S + dt B x, y = C.S + D x, gated = half(silu(z) * half(y)); the
+//          updated rows are stored back by bulk copies
 //       -- grid barrier --
 //       C  RMSNorm(gated) staged; out_proj work cut into (16-row tile, K chunk) units
 //          dealt round-robin over the SMs (every SM gets the same number +-1); each
@@ -41,8 +43,9 @@
 // The row -> SM assignments are the same in every layer and step, so each conv-state
 // and ssd-state row is only ever written by its owner SM.
 // Grid barriers are a monotonically increasing global counter (release add, acquire
-// spin) with a 2 s %globaltimer bound; every mbarrier wait is bounded too. A timeout
-// sets the error word and all CTAs leave after draining their in-flight copies.
+// spin) with a 2 s %globaltimer bound; every mbarrier wait and exchange-word poll is
+// bounded too. A timeout sets the error word; the consumer warps of a CTA decide to leave
+// together (a barrier that ORs the abort flag), and every CTA drains its in-flight copies.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -70,7 +73,7 @@ constexpr uint32_t TG = 5;                                // tiles per register-
 constexpr uint32_t XBUF = 20480;                          // staged activation (<= 2 x 5120 halves)
 constexpr uint32_t PART = TG * CONS_WARPS * 8 * 4 * 4;    // per-warp partial sums of one group ([ti][warp][g][4])
 constexpr uint32_t XSUM = 2 * 5120 / 32 * 4;              // per-block sums of the staged activation (fp32)
-constexpr uint32_t SBUF = 36864;                          // this CTA's ssd state rows (<= 72 x 128 fp32)
+constexpr uint32_t SBUF = 40960;                          // this CTA's ssd state rows (<= 80 x 128 fp32)
 constexpr uint32_t SROWS = SBUF / 512;
 constexpr uint32_t HBUF = 10240;                          // hidden vector(s) (B x d_model fp16)
 constexpr uint32_t BSLOTS = 4;                            // (seq, group) B / C vector slots in phase B
@@ -133,6 +136,19 @@ __device__ __forceinline__ bool mbar_wait_ab(uint32_t bar, uint32_t parity, vola
     }
 }
 
+// Barrier over the consumer threads that also ORs `c` across them: every consumer gets the
+// same answer, so decisions to leave (a bounded wait gave up somewhere) never diverge
+// between warps that must meet at the next barrier.
+__device__ __forceinline__ bool cons_any(bool c) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)c), "n"(CONS)
+        : "memory");
+    return r != 0;
+}
+
 // Grid barrier over the consumer threads of every CTA (the producer warp never joins).
 __device__ __forceinline__ bool grid_sync(const PParams& p, uint32_t& gen, volatile int* abort) {
     cons_sync();
@@ -154,8 +170,47 @@ __device__ __forceinline__ bool grid_sync(const PParams& p, uint32_t& gen, volat
             }
         }
     }
-    cons_sync();
-    return !*abort;
+    return !cons_any(*abort != 0);
+}
+
+// ---- exchange words: {32-bit payload, 32-bit epoch} stored as one 64-bit word, so a reader
+// that sees the epoch also sees the payload (no fence, no flag). Relaxed gpu-scope accesses
+// (L2, never a stale L1 line).
+__device__ __forceinline__ uint64_t mb_word(uint32_t payload, uint32_t tag) {
+    return ((uint64_t)tag << 32) | payload;
+}
+__device__ __forceinline__ void mb_put(uint64_t* a, uint64_t w) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t mb_ld(const uint64_t* a) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void mb_ld2(const uint64_t* a, uint64_t& x, uint64_t& y) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(a) : "memory");
+}
+__device__ __forceinline__ bool mb_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+// Slow path: re-reads one word until it carries `tag`. Gives up (returns a word whose tag is
+// wrong) on the CTA abort flag, on the device error word (another CTA gave up) or after 2 s,
+// setting both flags.
+__device__ __forceinline__ uint64_t mb_spin(const uint64_t* a, uint32_t tag, volatile int* abort, int* err) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 1;; ++it) {
+        const uint64_t w = mb_ld(a);
+        if (mb_ok(w, tag)) return w;
+        if ((it & 15) == 0) {
+            if (*abort) return w;
+            if (*reinterpret_cast<volatile int*>(err)) { *abort = 1; return w; }
+            const uint64_t t = gtimer();
+            if (!t0) t0 = t;
+            else if (t - t0 > SPIN_NS) { *abort = 1; atomicExch(err, 1); return w; }
+        }
+        __nanosleep(it < 8 ? 64 : 256);
+    }
+}
+__device__ __forceinline__ void mb_need(const uint64_t* a, uint32_t tag, uint64_t& w, volatile int* abort, int* err) {
+    if (!mb_ok(w, tag)) w = mb_spin(a, tag, abort, err);
 }
 
 // Swizzled shared-memory offset of 16-byte chunk `j` (0..7) of 128-byte segment `s` of
@@ -368,8 +423,9 @@ __device__ void stage_norm(const __half* src, uint64_t src_stride, const uint32_
 // the next layer; the normalised fp16 values go to xbuf as in stage_norm. Every SM
 // computes the same vector (same inputs, same order of additions). The residual pass
 // works on 4-element quads (<= NOCT per thread: K <= 2560), all slot loads in flight at once.
+template <uint32_t NB>
 __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* tok, const __half* embed, __half* hid,
-                             const __half* w, uint32_t M, uint32_t K, bool frag, uint8_t* xbuf, float* xsum, float* red) {
+                             const __half* w, uint32_t K, bool frag, uint8_t* xbuf, float* xsum, float* red) {
     const uint32_t tid = threadIdx.x, nq = K / 8, n4 = K / 4;
     uint4 wv[NOCT];
 #pragma unroll
@@ -377,31 +433,32 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
         const uint32_t q = tid + i * CONS;
         if (q < nq) wv[i] = __ldg(reinterpret_cast<const uint4*>(w) + q);
     }
-    for (uint32_t m = 0; m < M; ++m) {
+    // slots loaded two at a time (at most 2 x NOCT float4 loads in flight per thread)
+    constexpr uint32_t CB = 2;
+    for (uint32_t m = 0; m < NB; ++m) {
         __half* hrow = hid + (uint64_t)m * K;
         uint2 hv[NOCT];
         float4 o[NOCT];
-        // slots summed two at a time (c = 0, 1 then 2, 3): the same fixed order, and at
-        // most 6 float4 loads in flight per thread
+        // slots summed in chunk order c = 0, 1, 2, 3 (fixed)
 #pragma unroll
-        for (uint32_t c0 = 0; c0 < NCH_MAX; c0 += 2) {
+        for (uint32_t c0 = 0; c0 < NCH_MAX; c0 += CB) {
             if (tok || c0 >= nch) break;
-            float4 pa[NOCT][2];
+            float4 pa[NOCT][CB];
 #pragma unroll
             for (int i = 0; i < (int)NOCT; ++i) {
                 const uint32_t q = tid + i * CONS;
                 if (q >= n4) continue;
 #pragma unroll
-                for (uint32_t c = 0; c < 2; ++c)
+                for (uint32_t c = 0; c < CB; ++c)
                     if (c0 + c < nch)
-                        pa[i][c] = __ldcg(reinterpret_cast<const float4*>(opart + ((uint64_t)(c0 + c) * M + m) * K) + q);
+                        pa[i][c] = __ldcg(reinterpret_cast<const float4*>(opart + ((uint64_t)(c0 + c) * NB + m) * K) + q);
             }
 #pragma unroll
             for (int i = 0; i < (int)NOCT; ++i) {
                 const uint32_t q = tid + i * CONS;
                 if (q >= n4) continue;
 #pragma unroll
-                for (uint32_t c = 0; c < 2; ++c) {
+                for (uint32_t c = 0; c < CB; ++c) {
                     if (c0 + c >= nch) continue;
                     if (c0 + c == 0) o[i] = pa[i][0];
                     else { o[i].x += pa[i][c].x; o[i].y += pa[i][c].y; o[i].z += pa[i][c].z; o[i].w += pa[i][c].w; }
@@ -446,6 +503,39 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
     }
 }
 
+// In_proj work of CTA s (owner computes): channel units of 8 d_inner channels are dealt in
+// contiguous ranges, the first `extra` CTAs taking one more; the z rows and x rows of a unit
+// form one 16-row tile (two 8-row halves), so the CTA that runs the ssd rows of a channel
+// also computes its x and z. The "special" tiles hold the B, C and dt rows (16 rows at
+// 2 d_inner + 16 k); special tile k goes to CTA (extra + k) mod G, i.e. first to CTAs with
+// fewer units, and each CTA runs its special tiles before its units, so the rows every CTA
+// polls are written early.
+struct InTiles {
+    uint32_t ub, nu;      // first unit, units
+    uint32_t kfirst, nsp; // first special tile index, special tiles (k = kfirst + i * G)
+};
+__host__ __device__ __forceinline__ InTiles in_tiles(uint32_t s, uint32_t G, uint32_t di, uint32_t nspec) {
+    const uint32_t NU = di / 8, base = NU / G, extra = NU % G;
+    InTiles t;
+    t.nu = base + (s < extra ? 1u : 0u);
+    t.ub = s * base + (s < extra ? s : extra);
+    t.kfirst = (s + G - (extra % G)) % G;
+    t.nsp = t.kfirst < nspec ? (nspec - 1 - t.kfirst) / G + 1 : 0;
+    return t;
+}
+// Row starts of the two 8-row halves of tile ti of a CTA.
+__device__ __forceinline__ void in_tile_rows(const InTiles& t, uint32_t ti, uint32_t G, uint32_t di, uint32_t& h0,
+                                             uint32_t& h1) {
+    if (ti < t.nsp) {
+        h0 = 2 * di + 16 * (t.kfirst + ti * G);
+        h1 = h0 + 8;
+    } else {
+        const uint32_t u = t.ub + ti - t.nsp;
+        h0 = 8 * u;
+        h1 = di + 8 * u;
+    }
+}
+
 // First-max argmax step: (v, i) replaces (bv, bi) when larger, or equal with a lower index.
 __device__ __forceinline__ void argmax_take(float& bv, uint32_t& bi, float v, uint32_t i) {
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -480,7 +570,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     float* part = reinterpret_cast<float*>(smem + OFF_PART);
     float* xsum = reinterpret_cast<float*>(smem + OFF_XSUM);
     uint8_t* xbuf = smem + OFF_X;
-    const float* sstate = reinterpret_cast<const float*>(smem + OFF_S);
+    float* sstate = reinterpret_cast<float*>(smem + OFF_S);
     __half* hid = reinterpret_cast<__half*>(smem + OFF_H);
     __half* bcs = reinterpret_cast<__half*>(smem + OFF_BC);
     float* rowv = reinterpret_cast<float*>(smem + OFF_ROWV);
@@ -490,26 +580,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
-    const uint32_t nA = (p.proj + 15) / 16, nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
+    const uint32_t nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
     const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
     const uint32_t uC = nC * nchC;                                  // out_proj (tile, chunk) units
-    const uint32_t ntA = cta < nA ? (nA - 1 - cta) / G + 1 : 0;    // this CTA's in_proj tiles
+    const uint32_t nspec = (2 * p.G * p.N + p.H + 15) / 16;        // B / C / dt tiles
+    const InTiles tt = in_tiles(cta, G, p.di, nspec);
+    const uint32_t ntA = tt.nsp + tt.nu;                            // this CTA's in_proj tiles
     const uint32_t nuC = cta < uC ? (uC - 1 - cta) / G + 1 : 0;    // this CTA's out_proj units
     const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;    // lm_head tiles
-    const uint32_t srows = NB * p.H * p.P;
-    const uint32_t r0 = (uint32_t)(((uint64_t)srows * cta) / G), r1 = (uint32_t)(((uint64_t)srows * (cta + 1)) / G);
-    const uint32_t nrows = r1 - r0;
+    // state rows: the channels of this CTA's units, for each sequence (local row j: sequence
+    // j / (8 nu), channel 8 ub + j % (8 nu))
+    const uint32_t urows = 8 * tt.nu, nrows = NB * urows;
     const uint32_t GN = p.G * p.N, hpg = p.H / p.G;
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
     if (p.dconv > 4 || p.dconv < 1 || NB > 2 || NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
-        (srows + G - 1) / G > SROWS ||
+        NB * 8 * ((p.di / 8 + G - 1) / G) > SROWS || p.di % 8 || p.H * p.P != p.di ||
         p.n_layer > LT_MAX || (uint64_t)NB * max(p.dm, p.di) * 2 > XBUF || (uint64_t)NB * p.dm * 2 > HBUF ||
         p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
         nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
-        p.H % p.G || ((nA + G - 1) / G) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
+        p.H % p.G || ((p.di / 8 + G - 1) / G + (nspec + G - 1) / G) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -525,7 +617,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         // distinct (seq, group) pairs of this CTA's state rows -> B / C slots
         uint32_t ns = 0;
         for (uint32_t j = 0; j < nrows; ++j) {
-            const uint32_t mh = (r0 + j) / p.P, key = (mh / p.H) * p.G + (mh % p.H) / hpg;
+            const uint32_t m = j / urows, c = 8 * tt.ub + j % urows, h = c / p.P, pp = c % p.P;
+            const uint32_t key = m * p.G + h / hpg;
             uint32_t sl = 0;
             while (sl < ns && skey[sl] != key) ++sl;
             if (sl == ns) {
@@ -534,7 +627,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             }
             rslot[j] = (uint8_t)sl;
             // (seq m, head h, channel pp) of the row, packed once: no divisions in phase B
-            const uint32_t m = mh / p.H, h = mh % p.H, pp = (r0 + j) % p.P;
             reinterpret_cast<uint32_t*>(rowv)[j * 6 + 5] = (m << 24) | (pp << 16) | h;
         }
         *nslot_s = ns;
@@ -567,6 +659,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 last_phase[slot] = (int)phase;
                 if (++slot == RING) { slot = 0; phase ^= 1; }
             };
+            // one in_proj (tile, chunk): two 8-row halves starting at rows h0 and h1
+            auto put_in = [&](const CUtensorMap* mw, uint32_t seg, uint32_t h0, uint32_t h1, uint32_t c) -> bool {
+                const uint32_t s = take();
+                if (s == ~0u) return false;
+                const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
+                const int32_t cs = (int32_t)(c * seg);
+                mbar_expect(bar, 16 * seg * (128 + 16));
+                tma3(dst, mw, 0, cs, (int32_t)h0, bar, pol);
+                tma3(dst + 8 * seg * 128, mw, 0, cs, (int32_t)h1, bar, pol);
+                tma2(dst + 16 * seg * 128, mw + 1, cs * 8, (int32_t)h0, bar, pol);
+                tma2(dst + 16 * seg * 128 + 8 * seg * 16, mw + 1, cs * 8, (int32_t)h1, bar, pol);
+                advance();
+                return true;
+            };
             // one INT4 (tile, chunk) unit: weights (3-D, swizzled) + scales (2-D)
             auto put_int4 = [&](const CUtensorMap* mw, uint32_t seg, uint32_t u, uint32_t nch) -> bool {
                 const uint32_t s = take();
@@ -589,7 +695,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     if (!mbar_wait_ab(smem_u32(sempty), sphase ^ 1, abort)) { ok = false; break; }
                     if (sbytes) {
                         mbar_expect(smem_u32(sfull), sbytes);
-                        bulk_g2s(smem_u32(smem + OFF_S), LT[l].ssd_state + (uint64_t)r0 * p.N, sbytes, smem_u32(sfull));
+                        for (uint32_t m = 0; m < NB; ++m)
+                            bulk_g2s(smem_u32(smem + OFF_S + m * urows * p.N * 4),
+                                     LT[l].ssd_state + ((uint64_t)m * p.di + 8 * tt.ub) * p.N, urows * p.N * 4,
+                                     smem_u32(sfull));
                     } else {
                         mbar_arrive1(smem_u32(sfull));
                     }
@@ -597,7 +706,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     sphase ^= 1;
                     for (uint32_t ti = 0; ti < ntA && ok; ++ti)
                         for (uint32_t c = 0; c < nchA && ok; ++c) {
-                            ok = put_int4(mp, p.seg_in, (cta + ti * G) * nchA + c, nchA);
+                            uint32_t h0, h1;
+                            in_tile_rows(tt, ti, G, p.di, h0, h1);
+                            ok = put_in(mp, p.seg_in, h0, h1, c);
                             if (p.trace && step == 0 && ti == 0 && c == 0)
                                 p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
                         }
@@ -635,15 +746,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     auto consume_group = [&](bool int4, uint32_t seg, uint32_t nch, uint32_t K, bool split, uint32_t i0,
                              uint32_t nt) -> bool {
         float acc[TG][4];
+        bool bad = false;   // a bounded ring wait gave up: skip the rest, leave together below
 #pragma unroll
         for (uint32_t ti = 0; ti < TG; ++ti) {
             acc[ti][0] = acc[ti][1] = acc[ti][2] = acc[ti][3] = 0.0f;
-            if (ti < nt) {
+            if (ti < nt && !bad) {
                 const uint32_t u = cta + (i0 + ti) * G;
                 const uint32_t c0 = split ? u % nch : 0, c1 = split ? c0 + 1 : nch;
                 for (uint32_t c = c0; c < c1; ++c) {
                     const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
-                    if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) return false;
+                    if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) { bad = true; break; }
                     if (p.trace && tid == 0) wait_ns += gtimer() - w0;
                     const uint8_t* stage = smem + OFF_RING + slot * STAGE;
                     if (int4)
@@ -674,8 +786,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 *reinterpret_cast<float4*>(part + ((ti * CONS_WARPS + warp) * 8 + (lane >> 2)) * 4) =
                     make_float4(v[0], v[1], v[2], v[3]);
         }
-        cons_sync();
-        return true;
+        return !cons_any(bad || *abort);
     };
     // Cross-warp sum of output (unit ordinal ti within the group, row, sequence m).
     auto reduce_item = [&](uint32_t ti, uint32_t row, uint32_t m) -> float {
@@ -703,9 +814,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     // Each thread owns one (tile ordinal, row, seq) output of in_proj for the epilogue.
     const uint32_t tiA = tid / (16 * NB), rowA = (tid / NB) % 16, mA = tid % NB;
     const bool ownA = tiA < ntA;
-    const uint32_t rA = (cta + tiA * G) * 16 + rowA;           // in_proj output row
+    uint32_t hA0 = 0, hA1 = 0;
+    if (ownA) in_tile_rows(tt, tiA, G, p.di, hA0, hA1);
+    const uint32_t rA = rowA < 8 ? hA0 + rowA : hA1 + rowA - 8;   // in_proj output row
     const bool convA = ownA && rA >= p.di && rA < p.di + p.xd;
     const uint32_t dA = rA - p.di;
+    const bool specA = tiA < tt.nsp;                               // B / C / dt rows: published
+    const uint32_t jA = mA * urows + (tiA - tt.nsp) * 8 + (rowA & 7);   // unit rows: local state row
 
     bool ok = true;
     for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
@@ -716,6 +831,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         for (uint32_t l = 0; l < p.n_layer && ok; ++l) {
             const PLayer& L = LT[l];
             const uint32_t lb = l * TRACE_PER_LAYER;
+            const uint32_t ep = p.epoch0 + step * p.n_layer + l;   // tag of this layer's in_proj exchange words
             stamp(lb + 0);
             wait_ns = 0;
             // ---- loads consumed only in this layer's in_proj epilogue (issued first, waited
@@ -732,18 +848,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 cbh = L.conv_b[dA];
             }
             // ---- A: residual + RMSNorm, in_proj tiles (all K chunks of a tile), epilogue:
-            // z / dt stored, xBC rows -> conv-state roll + conv + SiLU -> x, B, C
-            stage_norm_h(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, NB, p.dm, true, xbuf, xsum,
+            // z / dt and, for xBC rows, conv-state roll + conv + SiLU -> exchange words
+            stage_norm_h<NB>(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.dm, true, xbuf, xsum,
                          red);
             stamp(lb + 1);
-            for (uint32_t g0 = 0; g0 < ntA && ok; g0 += TG) {
-                const uint32_t nt = min(TG, ntA - g0);
+            // special tiles form their own group(s), so their rows are published before the units run
+            for (uint32_t g0 = 0, nt = 0; g0 < ntA && ok; g0 += nt) {
+                nt = g0 < tt.nsp ? min(TG, tt.nsp - g0) : min(TG, ntA - g0);
                 if (!consume_group(true, p.seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
                 if (ownA && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
-                    const __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
-                    if (!convA) {
-                        p.projb[(uint64_t)mA * p.proj + rA] = vh;          // z or dt
-                    } else {
+                    __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
+                    if (convA) {
                         // conv-state roll + depthwise conv + SiLU (k_conv_update_silu_split arithmetic)
                         __half* st = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
                         float acc = __half2float(cbh);
@@ -759,44 +874,55 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         for (uint32_t k = 1; k < 4; ++k)
                             if (k == p.dconv - 1) wl = cwh[k];
                         acc += __half2float(vh) * __half2float(wl);
-                        const __half o = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
-                        if (dA < p.di) p.xs[(uint64_t)mA * p.di + dA] = o;
-                        else if (dA < p.di + GN) p.Bs[(uint64_t)mA * GN + (dA - p.di)] = o;
-                        else p.Cs[(uint64_t)mA * GN + (dA - p.di - GN)] = o;
+                        vh = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
                     }
+                    if (specA) mb_put(p.mb_in + (uint64_t)mA * p.proj + rA, mb_word(__half_as_ushort(vh), ep));
+                    else rowv[jA * 6 + (rowA < 8 ? 4 : 3)] = __half2float(vh);   // z / x of an own row
                 }
                 cons_sync();   // partial sums reused by the next group
             }
             stamp(lb + 2);
             if (tr) p.trace[tbase + lb + 9] = wait_ns;   // warp 0's ring wait during in_proj
-            if (!ok || !grid_sync(p, gen, abort)) { ok = false; break; }
-            stamp(lb + 3);
-            // ---- B: ssd_step + gate over this CTA's state rows: B / C vectors of its
-            // (seq, group) slots and per-row scalars staged in one parallel round of loads
+            if (!ok) break;
+            // ---- B: ssd_step + gate over this CTA's state rows. No grid barrier: the B / C
+            // vectors of its (seq, group) slots and each row's x, z and dt are polled from the
+            // exchange words of this layer (one parallel round of loads, then re-reads of any
+            // word not yet written)
             {
                 if (tid < nslot * 64) {
                     const uint32_t sl = tid >> 6, w = tid & 63, key = skey[sl], m = key / p.G, g = key % p.G;
-                    const __half* src = (w < 32 ? p.Bs : p.Cs) + (uint64_t)m * GN + g * p.N + (w & 31) * 4;
+                    const uint64_t* a = p.mb_in + (uint64_t)m * p.proj + 2 * p.di + (w < 32 ? 0 : GN) + g * p.N +
+                                        (w & 31) * 4;
+                    uint64_t v[4];
+                    mb_ld2(a, v[0], v[1]);
+                    mb_ld2(a + 2, v[2], v[3]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) mb_need(a + j, ep, v[j], abort, p.err);
                     *reinterpret_cast<uint2*>(bcs + sl * 256 + (w < 32 ? 0 : 128) + (w & 31) * 4) =
-                        __ldcg(reinterpret_cast<const uint2*>(src));
+                        make_uint2((uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16),
+                                   (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16));
                 }
                 if (tid < nrows) {
+                    // x and z of the row came from this CTA's own in_proj epilogue (rv[3], rv[4])
                     const uint32_t info = reinterpret_cast<const uint32_t*>(rowv)[tid * 6 + 5];
-                    const uint32_t m = info >> 24, pp = (info >> 16) & 0xFF, h = info & 0xFFFF;
+                    const uint32_t m = info >> 24, h = info & 0xFFFF;
+                    const uint64_t* adt = p.mb_in + (uint64_t)m * p.proj + p.di + p.xd + h;   // dt (raw)
+                    uint64_t wdt = mb_ld(adt);
                     const float A = -expf(__half2float(L.A_log[h]));
-                    const float dt = fminf(fmaxf(softplus(__half2float(__ldcg(p.projb + (uint64_t)m * p.proj + p.di + p.xd + h)) +
-                                                          __half2float(L.dt_bias[h])), 1e-6f), 1e6f);
-                    const float xv = __half2float(__ldcg(p.xs + (uint64_t)m * p.di + h * p.P + pp));
+                    const float dtb = __half2float(L.dt_bias[h]), Dh = __half2float(L.D[h]);
+                    mb_need(adt, ep, wdt, abort, p.err);
+                    const float dt =
+                        fminf(fmaxf(softplus(__half2float(__ushort_as_half((uint16_t)wdt)) + dtb), 1e-6f), 1e6f);
                     float* rv = rowv + tid * 6;
+                    const float xv = rv[3];
                     rv[0] = expf(A * dt);
                     rv[1] = dt * xv;
-                    rv[2] = __half2float(L.D[h]);
-                    rv[3] = xv;
-                    rv[4] = __half2float(__ldcg(p.projb + (uint64_t)m * p.proj + h * p.P + pp));
+                    rv[2] = Dh;
                 }
-                if (!mbar_wait_ab(smem_u32(sfull), sphase, abort)) { ok = false; break; }
+                const bool sbad = !mbar_wait_ab(smem_u32(sfull), sphase, abort);
                 sphase ^= 1;
-                cons_sync();
+                if (cons_any(sbad || *abort)) { ok = false; break; }
+                stamp(lb + 3);
                 for (uint32_t j0 = warp; j0 < nrows; j0 += 2 * CONS_WARPS) {
                     float a2[2];
                     float4 v2[2];
@@ -829,12 +955,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     for (int q = 0; q < 2; ++q) {
                         const uint32_t j = j0 + q * CONS_WARPS;
                         if (j >= nrows) continue;
-                        const uint32_t row = r0 + j;
-                        *reinterpret_cast<float4*>(L.ssd_state + (uint64_t)row * p.N + lane * 4) = v2[q];
+                        const float* rv = rowv + j * 6;
+                        const uint32_t info = reinterpret_cast<const uint32_t*>(rv)[5];
+                        const uint32_t m = info >> 24, pp = (info >> 16) & 0xFF, h = info & 0xFFFF;
+                        // the new state goes back into the shared buffer; one bulk copy per
+                        // sequence stores the rows after the loop
+                        *reinterpret_cast<float4*>(sstate + (uint64_t)j * p.N + lane * 4) = v2[q];
                         if (lane == 0) {
-                            const float* rv = rowv + j * 6;
-                            const uint32_t info = reinterpret_cast<const uint32_t*>(rv)[5];
-                            const uint32_t m = info >> 24, pp = (info >> 16) & 0xFF, h = info & 0xFFFF;
                             const float yh = __half2float(__float2half_rn(a2[q] + rv[2] * rv[3]));
                             p.gated[(uint64_t)m * p.di + h * p.P + pp] = __float2half_rn(silu(rv[4]) * yh);
                         }
@@ -842,11 +969,23 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 }
             }
             if (!ok) break;
-            // the state rows written above are read back by a later bulk copy (async proxy)
-            asm volatile("fence.proxy.async.global;" ::: "memory");
+            // the updated state rows (shared memory, generic proxy) are stored by the async proxy:
+            // bulk copies issued here, not waited for by the grid barrier's fence, and completed
+            // before the buffer is handed back to the producer
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            cons_sync();
+            if (tid == 0 && urows) {
+                for (uint32_t m = 0; m < NB; ++m)
+                    bulk_s2g(L.ssd_state + ((uint64_t)m * p.di + 8 * tt.ub) * p.N,
+                             smem_u32(smem + OFF_S + m * urows * p.N * 4), urows * p.N * 4);
+                bulk_commit();
+            }
             stamp(lb + 4);
             if (!grid_sync(p, gen, abort)) { ok = false; break; }
-            if (tid == 0) mbar_arrive1(smem_u32(sempty));   // all reads of the state buffer are done
+            if (tid == 0) {
+                bulk_wait_all();
+                mbar_arrive1(smem_u32(sempty));   // state stored; the buffer may be refilled
+            }
             stamp(lb + 5);
             // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
             stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, NB, p.di, true, xbuf, xsum, red);
@@ -859,7 +998,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         if (!ok) break;
         // ---- residual + norm_f + lm_head + first-max argmax partials
         wait_ns = 0;
-        stage_norm_h(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, NB, p.dm, false, xbuf, xsum, red);
+        stage_norm_h<NB>(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.dm, false, xbuf, xsum, red);
         stamp(lmb + 0);
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
@@ -921,6 +1060,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         }
         stamp(lmb + 3);
     }
+    if (tid == 0) bulk_wait_all();   // no state store still reading shared memory at exit
     if (!ok) {
         *abort = 1;
         if (tid == 0) atomicExch(p.err, 1);
@@ -958,13 +1098,14 @@ uint32_t odd_seg(uint32_t total) {
 // [rows][segs][128 B] view of a row-major matrix with `row_bytes` per row; box = 16 rows
 // x seg segments, 128-byte swizzle; f16 selects the element type (fp16 rows, or bytes
 // holding INT4 nibble pairs).
-bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t seg, bool f16) {
+bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t seg, bool f16,
+              uint32_t box_rows = 16) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     const uint64_t esz = f16 ? 2 : 1;
     cuuint64_t dims[3] = {128 / esz, row_bytes / 128, rows};
     cuuint64_t strides[2] = {128, row_bytes};
-    cuuint32_t box[3] = {(cuuint32_t)(128 / esz), seg, 16};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / esz), seg, box_rows};
     cuuint32_t estr[3] = {1, 1, 1};
     return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base),
                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -972,12 +1113,12 @@ bool map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_byte
 }
 
 // INT4_B32 scales [rows][K/32] fp16; box = 16 rows x seg*8 scales, no swizzle.
-bool map_scales(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t seg) {
+bool map_scales(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t seg, uint32_t box_rows = 16) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[2] = {K / 32, rows};
     cuuint64_t strides[1] = {K / 16};
-    cuuint32_t box[2] = {seg * 8, 16};
+    cuuint32_t box[2] = {seg * 8, box_rows};
     cuuint32_t estr[2] = {1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -998,10 +1139,12 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     if ((uint64_t)sh.B * (sh.dm > sh.di ? sh.dm : sh.di) * 2 > XBUF) return "staged activations exceed 20 KB";
     if (sh.n_layer > LT_MAX) return "more than 64 layers";
     if ((uint64_t)sh.B * sh.dm * 2 > HBUF) return "hidden vectors exceed 10 KB";
-    if (((sh.proj + 15) / 16 + G - 1) / G * 16 * sh.B > CONS) return "too many in_proj rows per SM";
+    if (sh.di % 8 || sh.H * sh.P != sh.di) return "d_inner must be n_heads x d_head, a multiple of 8";
+    const uint32_t nspec = (2 * sh.G * sh.N + sh.H + 15) / 16;
+    if (((sh.di / 8 + G - 1) / G + (nspec + G - 1) / G) * 16 * sh.B > CONS) return "too many in_proj rows per SM";
     if (sh.dm / 4 > NOCT * CONS) return "d_model too wide for the residual pass (<= 2560)";
     if (sh.H % sh.G) return "n_heads not divisible by n_groups";
-    if (((uint64_t)sh.B * sh.H * sh.P + G - 1) / G > SROWS) return "ssd state rows per SM exceed 36 KB";
+    if ((uint64_t)sh.B * 8 * ((sh.di / 8 + G - 1) / G) > SROWS) return "ssd state rows per SM exceed 40 KB";
     *seg_in = odd_seg(sh.dm / 256);
     *seg_out = odd_seg(sh.di / 256);
     *seg_lm = odd_seg(sh.dm / 64);
@@ -1017,8 +1160,9 @@ bool decode_persist_encode_maps(void* out, const PLayer* layers, const void* lm_
     for (uint32_t l = 0; l < sh.n_layer; ++l) {
         const uint8_t* in_w = layers[l].in_w;
         const uint8_t* out_w = layers[l].out_w;
-        if (!map_rows(&m[4 * l + 0], in_w, sh.proj, sh.dm / 2, seg_in, false) ||
-            !map_scales(&m[4 * l + 1], in_w + (size_t)sh.proj * sh.dm / 2, sh.proj, sh.dm, seg_in) ||
+        // in_proj: 8-row boxes (a stage holds two 8-row halves: z / x rows of one channel unit)
+        if (!map_rows(&m[4 * l + 0], in_w, sh.proj, sh.dm / 2, seg_in, false, 8) ||
+            !map_scales(&m[4 * l + 1], in_w + (size_t)sh.proj * sh.dm / 2, sh.proj, sh.dm, seg_in, 8) ||
             !map_rows(&m[4 * l + 2], out_w, sh.dm, sh.di / 2, seg_out, false) ||
             !map_scales(&m[4 * l + 3], out_w + (size_t)sh.dm * sh.di / 2, sh.dm, sh.di, seg_out))
             return false;

@@ -147,9 +147,15 @@ struct PLayer {
 struct PParams {
     const PLayer* layers; uint32_t n_layer;
     const __half* embed; const __half* norm_f; const __half* lm_head;
-    __half* projb; __half* xs; __half* Bs; __half* Cs;   // in_proj outputs: [z | . | dt], x, B, C (fp16)
+    // in_proj outputs for the ssd phase as exchange words [B][proj], each {fp16 bits, 32-bit
+    // epoch} in one 64-bit store (z, x / B / C after conv + SiLU, dt), so data and readiness
+    // travel together and a reader polls only the words it needs. Layer l of step t carries
+    // epoch epoch0 + t * n_layer + l.
+    uint64_t* mb_in;
+    uint32_t epoch0;
     float* opart;                            // out_proj partial sums [chunk][seq][d_model] fp32
-    __half* gated; __half* logits;
+    __half* gated;
+    __half* logits;
     float* part_val; uint32_t* part_idx;     // (gridDim, B)
     uint32_t* cur; uint32_t* history; uint32_t hist_stride; uint32_t n_steps;
     uint32_t* bar; int* err;

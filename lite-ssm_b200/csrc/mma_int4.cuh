@@ -73,6 +73,16 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                  : "memory");
 }
 
+// Non-tensor bulk copy shared -> global in the thread's bulk async-group (16-B aligned,
+// size % 16 == 0); bulk_commit closes the group, bulk_wait_all waits for every group to complete.
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // mbarrier phase wait that gives up after 2 s of %globaltimer.
 __device__ __forceinline__ bool bar_wait_bounded(uint32_t bar, uint32_t parity) {
     uint32_t ok = 0;
