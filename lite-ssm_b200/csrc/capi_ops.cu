@@ -90,6 +90,19 @@ static lssm_status scratch_reserve(lssm_ctx* ctx, size_t n, void** out) {
     return LSSM_OK;
 }
 
+// Scratch for an optional fast path: the context's scratch when it already holds n bytes, or
+// after growing it outside a capture; nullptr (no error recorded) when it cannot be had, and
+// the op then takes its path without scratch.
+static void* scratch_try(lssm_ctx* ctx, size_t n) {
+    if (ctx->scratch_size < n && ctx->capturing) return nullptr;
+    void* p = nullptr;
+    if (scratch_reserve(ctx, n, &p) != LSSM_OK) {
+        set_error("");
+        return nullptr;
+    }
+    return p;
+}
+
 // Frees the scratch blocks only the (now replaced or destroyed) kept graph referred to.
 static void scratch_release_retired(lssm_ctx* ctx) {
     if (ctx->scratch_retired.empty()) return;
@@ -496,6 +509,9 @@ lssm_status lssm_ssd_chunked_f16(lssm_ctx* ctx, const void* X, size_t X_off, con
     a.batch = 1; a.L = d.L; a.H = d.H; a.P = d.P; a.N = d.N; a.G = d.n_groups ? d.n_groups : 1; a.chunk = d.chunk_size;
     a.dt_min = d.dt_min; a.dt_max = d.dt_max; a.has_D = d.has_D;
     a.x_dtype = 0; a.dt_dtype = 0; a.param_dtype = 0; a.y_dtype = 0;
+    a.ws_bytes = ssd_chunked_cp_scratch(a.batch, a.H);
+    a.ws = scratch_try(ctx, a.ws_bytes);
+    a.sm_count = ctx->sm_count;
     LAUNCH("ssd_chunked_f16", launch_ssd_chunked(a, ctx->stream));
 }
 
@@ -522,6 +538,9 @@ lssm_status lssm_ssd_chunked_batched(lssm_ctx* ctx, const void* X, const void* B
     a.batch = d.batch; a.L = d.L; a.H = d.H; a.P = d.P; a.N = d.N; a.G = d.n_groups ? d.n_groups : 1;
     a.chunk = d.chunk_size; a.dt_min = d.dt_min; a.dt_max = d.dt_max; a.has_D = d.has_D;
     a.x_dtype = d.x_dtype; a.dt_dtype = d.dt_dtype; a.param_dtype = d.param_dtype; a.y_dtype = d.y_dtype;
+    a.ws_bytes = ssd_chunked_cp_scratch(a.batch, a.H);
+    a.ws = scratch_try(ctx, a.ws_bytes);
+    a.sm_count = ctx->sm_count;
     LAUNCH("ssd_chunked_batched", launch_ssd_chunked(a, ctx->stream));
 }
 

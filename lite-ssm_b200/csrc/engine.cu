@@ -895,9 +895,13 @@ static lssm_status session_alloc(lssm_session* s, uint32_t batch, uint32_t max_L
         if (L.out_dt == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)h.d_model * s->di); }
     }
     if (s->lm_dt == DT_INT4_B32) { any_int4 = true; wmax = std::max<size_t>(wmax, (size_t)s->V * h.d_model); }
-    if (any_int4) {
-        SA(s->wscratch, wmax * 2, "session: dequant scratch");
-        s->wscratch_elems = wmax;
+    // dequant scratch of the INT4 prefill GEMMs; also the carried-state ring of the
+    // chunk-parallel SSD scan, which runs while no GEMM uses it
+    size_t wbytes = any_int4 ? wmax * 2 : 0;
+    if (h.d_head == 64 && h.d_state == 128) wbytes = std::max(wbytes, ssd_chunked_cp_scratch(batch, s->H));
+    if (wbytes) {
+        SA(s->wscratch, wbytes, "session: dequant / scan scratch");
+        s->wscratch_elems = wbytes / 2;
     }
 #undef SA
     for (auto& e : s->ev) cudaEventCreate(&e);
@@ -1086,6 +1090,11 @@ static lssm_status run_block(lssm_session* s, uint32_t layer, uint32_t L, bool d
         a.dt_min = 1e-6f; a.dt_max = 1e6f; a.has_D = 1;
         a.x_dtype = 0; a.dt_dtype = 0; a.param_dtype = 0; a.y_dtype = 0;
         a.x_row_stride = di; a.bc_row_stride = GN; a.dt_row_stride = proj; a.y_row_stride = di;
+        // the chunk-parallel scan keeps its carried states in the dequant scratch, idle between
+        // the in_proj and out_proj GEMMs
+        a.ws_bytes = ssd_chunked_cp_scratch(B, H);
+        if (s->wscratch && s->wscratch_elems * 2 >= a.ws_bytes) a.ws = s->wscratch;
+        a.sm_count = s->ctx->sm_count;
         CU(launch_ssd_chunked(a, st));
         s->nl += 2;
     }

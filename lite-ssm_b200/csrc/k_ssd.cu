@@ -288,8 +288,13 @@ cudaError_t launch_ssd_chunked_tc(const SsdArgs& s, cudaStream_t st);
 cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s) {
     if (!a.batch || !a.L || !a.H) return cudaSuccess;
     // P = 64, N = 128 (every Mamba-2 checkpoint shape) with 16-byte aligned rows takes the
-    // tensor-core kernel; anything else uses the general-shape kernel below.
-    cudaError_t e = launch_ssd_chunked_tc(a, s);
+    // chunk-parallel tensor-core kernel when scratch for its carried states is given (and the
+    // heads pair up within groups), else the sequential tensor-core kernel; anything else
+    // uses the general-shape kernel below.
+    cudaError_t e = cudaErrorNotSupported;
+    if (a.ws) e = launch_ssd_chunked_cp(a, a.ws, a.ws_bytes, a.sm_count ? a.sm_count : 148, s);
+    if (e != cudaErrorNotSupported) return e;
+    e = launch_ssd_chunked_tc(a, s);
     if (e != cudaErrorNotSupported) return e;
     const size_t smem = sizeof(float) * ((size_t)a.P * a.N + 2ull * SSD_Q * a.N + (size_t)SSD_Q * a.P +
                                          (size_t)SSD_Q * SSD_Q + 3 * SSD_Q);

@@ -114,8 +114,15 @@ struct SsdArgs {
     // Y receives the gated half(silu(z) * half(y)) instead of y (mamba2_block.cpp:231-234).
     const void* z = nullptr;
     uint64_t z_row_stride = 0;
+    // Optional scratch of the chunk-parallel scan (carried-state ring + counters,
+    // ssd_chunked_cp_scratch bytes); without it the sequential tensor-core scan runs.
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int sm_count = 0;
 };
 cudaError_t launch_ssd_chunked(const SsdArgs& a, cudaStream_t s);
+size_t ssd_chunked_cp_scratch(uint32_t batch, uint32_t H);
+cudaError_t launch_ssd_chunked_cp(const SsdArgs& s, void* ws, size_t ws_bytes, int sm_count, cudaStream_t st);
 // out[r][c] = half(silu(z[r * z_stride + c]) * y[r][c]) over rows x d (y and out dense; may alias).
 cudaError_t launch_gate(const void* z, uint64_t z_stride, const void* y, void* out, uint32_t rows, uint32_t d,
                         cudaStream_t s);
