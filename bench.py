@@ -15,6 +15,11 @@ synchronize; prefill and decode are timed with CUDA events on the engine's strea
 max over ranks is reported. `e2e` repeats the request through the C ABI call with the
 prompt in pinned host memory and the generated ids copied back, timed on the host.
 
+The default line also carries `sharded_workloads`: at every N, on the same ranks, the two
+workloads that shard across GPUs (strong scaling, 1 warm-up + 2 timed steps each): the
+64-sequence batched decode with the sequences split over the GPUs, and the 8B shape with
+its heads tensor-parallel over all N GPUs (TP8 at N = 8).
+
 --impl reference times the reference's math on the host CPU (the reference has no CPU
 compute path of its own: its kernels are Metal shaders; the oracle under oracle/ is the
 C++ restatement of them) on a bounded sample of the same workload.
@@ -414,6 +419,22 @@ def run_ours(args, world, rank, local, dist):
     launches = args.steps * (n_pre + n_dec)   # n_dec: launches of the whole decode call
     prefill_flops = 2 * PROMPT * (HP27["n_layer"] * ((2 * 5120 + 256 + 80) * 2560 + 2560 * 5120))
 
+    # the workloads that shard across GPUs, measured at every N on the same ranks (collective):
+    # batched decode (sequences split over the GPUs) and the 8B shape (heads tensor-parallel)
+    sharded = None
+    if not args.no_sharded:
+        bl = run_batched(args, world, rank, local, dist, ctx=ctx, model=model, steps=2, warmup=1, emit=False)
+        tl = run_tp8b(args, world, rank, local, dist, ctx=ctx, steps=2, warmup=1, emit=False)
+        if rank == 0:
+            def brief(r):
+                return {"value": r["value"], "unit": r["unit"], "scaling": r["scaling"],
+                        "prefill_tok_s": r["prefill_tok_s"], "decode_ms_per_step": r["decode_ms_per_step"],
+                        "roofline_frac": r["roofline"]["frac"], "bytes_per_step_per_gpu": r["roofline"][
+                            "bytes_per_step_per_gpu"], "e2e": r["e2e"], "steps": r["steps"], "warmup": r["warmup"],
+                        "workload": r["config"]["workload"], "parallelism": r["config"]["parallelism"],
+                        "clocks": r["clocks"]}
+            sharded = {"batched": brief(bl), "tp8b": brief(tl)}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -447,6 +468,8 @@ def run_ours(args, world, rank, local, dist):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": NEW * 4},
             "gpu_launches": launches, "clocks": clk, "wall_s": wall,
         }
+        if sharded is not None:
+            line["sharded_workloads"] = sharded
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_baseline_sample(prompt=args.ref_prompt, new=args.ref_new)
             line["cpu_baseline"] = {"value": cb["decode_tok_s"], "unit": "tok/s", "cores": cb["cores"], "kind": "port",
@@ -623,10 +646,12 @@ def run_kernel_bench(args):
     return 0
 
 
-def run_batched(args, world, rank, local, dist):
+def run_batched(args, world, rank, local, dist, ctx=None, model=None, steps=None, warmup=None, emit=True):
     """Batched decode (the batched benchmark config): `--seqs` independent sequences (default
     64), each a 512-token prompt + 256 greedy decode steps, sharded over the ranks (seqs /
-    world per GPU, weights replicated, no data-path collective): strong scaling."""
+    world per GPU, weights replicated, no data-path collective): strong scaling. With `model`
+    given (the default run embeds this workload) it reuses that 2.7B model; returns the
+    record (rank 0) and prints it when `emit`."""
     import lssm
     import torch
     hbm, _, _, peak_kind = measured_peaks()
@@ -635,8 +660,13 @@ def run_batched(args, world, rank, local, dist):
         raise SystemExit(f"--seqs {total} is not divisible by {world} ranks")
     per = total // world
     plen, steps_new = args.batched_prompt, args.batched_new
-    ctx = lssm.Ctx(local)
-    model = lssm.Model.synthesize(ctx, lssm.hparams(**HP27), seed=0, int4=True)
+    n_steps = args.steps if steps is None else steps
+    n_warm = args.warmup if warmup is None else warmup
+    own = model is None
+    if ctx is None:
+        ctx = lssm.Ctx(local)
+    if own:
+        model = lssm.Model.synthesize(ctx, lssm.hparams(**HP27), seed=0, int4=True)
     sess = lssm.Session(ctx, model, batch=per, max_seq_len=plen)
     rng = np.random.default_rng(2000 + rank)
     prompts = rng.integers(0, VOCAB_IDS, size=(per, plen)).astype(np.uint32)
@@ -651,14 +681,14 @@ def run_batched(args, world, rank, local, dist):
 
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(args.warmup):
+    for _ in range(n_warm):
         step()
     barrier(dist, local)
     torch.cuda.synchronize()
     clocks.mark_begin()
     pre, dec = [], []
     w0 = time.time()
-    for _ in range(args.steps):
+    for _ in range(n_steps):
         p_ms, d_ms = step()
         pre.append(p_ms)
         dec.append(d_ms)
@@ -667,8 +697,8 @@ def run_batched(args, world, rank, local, dist):
     barrier(dist, local)
     clk = clocks.stop()
     tot_pre, tot_dec = allreduce_max(dist, [sum(pre), sum(dec)], local)
-    decode_tok_s = total * steps_new * args.steps / (tot_dec / 1000.0)
-    prefill_tok_s = total * plen * args.steps / (tot_pre / 1000.0)
+    decode_tok_s = total * steps_new * n_steps / (tot_dec / 1000.0)
+    prefill_tok_s = total * plen * n_steps / (tot_pre / 1000.0)
     # e2e: the same requests through lssm_generate, prompts from pinned host memory
     pinned = torch.from_numpy(prompts).pin_memory().numpy()
     barrier(dist, local)
@@ -681,12 +711,12 @@ def run_batched(args, world, rank, local, dist):
     state_b = HP27["n_layer"] * (bpt["per_layer"]["ssd_state_rw"] + bpt["per_layer"]["conv_state_rw"])
     step_bytes = (bpt["total"] - HP27["n_layer"] * (bpt["per_layer"]["ssd_state_rw"] + bpt["per_layer"]["conv_state_rw"])
                   + per * state_b)   # weights once per step per GPU + every sequence's state R+W
-    ms_step = tot_dec / args.steps / steps_new
+    ms_step = tot_dec / n_steps / steps_new
     n_pre, n_dec = sess.launches()
     if rank == 0:
         line = {
-            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": (tot_pre + tot_dec) / args.steps, "higher_is_better": True,
+            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": n_steps,
+            "warmup": n_warm, "ms_per_step": (tot_pre + tot_dec) / n_steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 activations, int4_b32 weights, f32 accum",
             "data": "synthetic (seeded random-init weights in the reference .ssm INT4_B32 layout, random prompt ids)",
             "config": {"workload": f"batched decode: {total} sequences x ({plen} prompt + {steps_new} greedy steps)",
@@ -701,15 +731,17 @@ def run_batched(args, world, rank, local, dist):
                          "peak_kind": f"{peak_kind} hbm_gbs"},
             "e2e": {"value": total * (steps_new + 1) / e_max, "unit": "tok/s", "h2d_bytes_per_step": per * plen * 4,
                     "d2h_bytes_per_step": per * (steps_new + 1) * 4},
-            "gpu_launches": args.steps * (n_pre + n_dec), "clocks": clk, "wall_s": wall,
+            "gpu_launches": n_steps * (n_pre + n_dec), "clocks": clk, "wall_s": wall,
         }
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
     sess.close()
-    model.close()
-    return 0
+    if own:
+        model.close()
+    return line if rank == 0 else None
 
 
-def run_tp8b(args, world, rank, local, dist):
+def run_tp8b(args, world, rank, local, dist, ctx=None, steps=None, warmup=None, emit=True):
     """The 8B-shape config: 4 sequences, prefill 4096 random ids + 128 greedy decode tokens,
     the heads (and groups, d_inner channels, lm_head vocab rows) tensor-parallel over the
     ranks with NCCL all-reduces after out_proj (and of the gated-norm sum of squares);
@@ -718,7 +750,10 @@ def run_tp8b(args, world, rank, local, dist):
     import torch
     hbm, _, _, peak_kind = measured_peaks()
     B, plen, steps_new = args.tp_batch, args.tp_prompt, args.tp_new
-    ctx = lssm.Ctx(local)
+    n_steps = args.steps if steps is None else steps
+    n_warm = args.warmup if warmup is None else warmup
+    if ctx is None:
+        ctx = lssm.Ctx(local)
     model = lssm.Model.synthesize(ctx, lssm.hparams(**HP8B), seed=0, int4=True)
     comm = None
     if world > 1:
@@ -741,14 +776,14 @@ def run_tp8b(args, world, rank, local, dist):
 
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(args.warmup):
+    for _ in range(n_warm):
         step()
     barrier(dist, local)
     torch.cuda.synchronize()
     clocks.mark_begin()
     pre, dec = [], []
     w0 = time.time()
-    for _ in range(args.steps):
+    for _ in range(n_steps):
         p_ms, d_ms, toks = step()
         pre.append(p_ms)
         dec.append(d_ms)
@@ -757,8 +792,8 @@ def run_tp8b(args, world, rank, local, dist):
     barrier(dist, local)
     clk = clocks.stop()
     tot_pre, tot_dec = allreduce_max(dist, [sum(pre), sum(dec)], local)
-    decode_tok_s = B * steps_new * args.steps / (tot_dec / 1000.0)
-    prefill_tok_s = B * plen * args.steps / (tot_pre / 1000.0)
+    decode_tok_s = B * steps_new * n_steps / (tot_dec / 1000.0)
+    prefill_tok_s = B * plen * n_steps / (tot_pre / 1000.0)
     pinned = torch.from_numpy(prompts).pin_memory().numpy()
     barrier(dist, local)
     t0 = time.perf_counter()
@@ -769,12 +804,12 @@ def run_tp8b(args, world, rank, local, dist):
     bpt = decode_bytes_per_token(HP8B)
     state_b = HP8B["n_layer"] * (bpt["per_layer"]["ssd_state_rw"] + bpt["per_layer"]["conv_state_rw"])
     step_bytes = (bpt["total"] - state_b + B * state_b) / world   # weights once per step + B states, per GPU
-    ms_step = tot_dec / args.steps / steps_new
+    ms_step = tot_dec / n_steps / steps_new
     n_pre, n_dec = sess.launches()
     if rank == 0:
         line = {
-            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": (tot_pre + tot_dec) / args.steps, "higher_is_better": True,
+            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s", "n_gpus": world, "steps": n_steps,
+            "warmup": n_warm, "ms_per_step": (tot_pre + tot_dec) / n_steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 activations, int4_b32 weights, f32 accum",
             "data": "synthetic (seeded random-init weights in the reference .ssm INT4_B32 layout, random prompt ids)",
             "config": {"workload": f"8B-shape: batch {B}, prefill {plen} + {steps_new} greedy decode tokens",
@@ -791,14 +826,15 @@ def run_tp8b(args, world, rank, local, dist):
                          "peak_kind": f"{peak_kind} hbm_gbs"},
             "e2e": {"value": B * (steps_new + 1) / e_max, "unit": "tok/s", "h2d_bytes_per_step": B * plen * 4,
                     "d2h_bytes_per_step": B * (steps_new + 1) * 4},
-            "gpu_launches": args.steps * (n_pre + n_dec), "clocks": clk, "wall_s": wall,
+            "gpu_launches": n_steps * (n_pre + n_dec), "clocks": clk, "wall_s": wall,
         }
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
     sess.close()
     if comm is not None:
         comm.close()
     model.close()
-    return 0
+    return line if rank == 0 else None
 
 
 def main():
@@ -833,6 +869,8 @@ def main():
     ap.add_argument("--ref-prompt", type=int, default=32)
     ap.add_argument("--ref-new", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the batched / tensor-parallel workloads the default run also measures")
     ap.add_argument("--prompt-len", type=int, default=PROMPT,
                     help="prompt tokens per request (the metric's workload is 2048; smaller only for profiling)")
     ap.add_argument("--decode-tokens", type=int, default=NEW,
@@ -850,9 +888,11 @@ def main():
     world, rank, local, dist = dist_setup(args.gpus)
     try:
         if args.workload == "batched":
-            return run_batched(args, world, rank, local, dist)
+            run_batched(args, world, rank, local, dist)
+            return 0
         if args.workload == "tp8b":
-            return run_tp8b(args, world, rank, local, dist)
+            run_tp8b(args, world, rank, local, dist)
+            return 0
         return run_ours(args, world, rank, local, dist)
     finally:
         if dist is not None:
