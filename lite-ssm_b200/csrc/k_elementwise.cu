@@ -51,9 +51,60 @@ __global__ void __launch_bounds__(256) k_rmsnorm_f16(const __half* __restrict__ 
     }
 }
 
+// 16-byte form: dim % 8 == 0, dim / 8 <= 4 * blockDim; each thread keeps its (<= 4) octets of the
+// row in registers between the sum of squares and the scaling (one read of x, one write of y).
+__global__ void __launch_bounds__(256) k_rmsnorm_f16_v8(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                        __half* __restrict__ y, uint32_t dim, float eps) {
+    __shared__ float red[32];
+    const uint64_t row = blockIdx.x;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * dim);
+    uint4* yr = reinterpret_cast<uint4*>(y + row * dim);
+    const uint32_t n8 = dim / 8;
+    uint4 xv[4];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t q = threadIdx.x + i * blockDim.x;
+        if (q < n8) xv[i] = xr[q];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t q = threadIdx.x + i * blockDim.x;
+        if (q >= n8) continue;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&xv[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h2[j]);
+            ss += f.x * f.x + f.y * f.y;
+        }
+    }
+    const float rrms = rsqrtf(block_sum(ss, red) / (float)dim + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t q = threadIdx.x + i * blockDim.x;
+        if (q >= n8) continue;
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + q);
+        const __half* xh = reinterpret_cast<const __half*>(&xv[i]);
+        const __half* wh = reinterpret_cast<const __half*>(&wv);
+        uint4 o;
+        __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) oh[j] = __float2half_rn(__half2float(xh[j]) * __half2float(wh[j]) * rrms);
+        yr[q] = o;
+    }
+}
+
 cudaError_t launch_rmsnorm_f16(const void* x, const void* w, void* y, uint32_t rows, uint32_t dim, float eps,
                                cudaStream_t s) {
     if (rows == 0 || dim == 0) return cudaSuccess;
+    if (dim % 8 == 0 && aligned(x, 16) && aligned(w, 16) && aligned(y, 16) && dim / 8 <= 4 * 256) {
+        uint32_t threads = (dim / 8 + 3) / 4;                 // <= 4 octets per thread
+        threads = (threads + 31) / 32 * 32;
+        threads = threads < 64 ? (dim / 8 < 64 ? (dim / 8 + 31) / 32 * 32 : 64) : threads;
+        k_rmsnorm_f16_v8<<<rows, threads, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(w),
+                                                  static_cast<__half*>(y), dim, eps);
+        return cudaGetLastError();
+    }
     const int vec = aligned(x, 4) && aligned(w, 4) && aligned(y, 4) && (dim % 2 == 0);
     uint32_t threads = (dim / 2 + 31) / 32 * 32;
     threads = threads < 32 ? 32 : (threads > 256 ? 256 : threads);

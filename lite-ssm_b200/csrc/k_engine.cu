@@ -71,7 +71,8 @@ __global__ void k_conv_silu_split(const __half* __restrict__ xbc, uint64_t in_st
 // Vectorised form (d_conv == 4, 8 channels per thread, 16-byte loads and stores): the
 // same arithmetic per channel. Needs in_stride, d_inner and GN multiples of 8 and 16-byte
 // aligned rows, so an octet never straddles the x / B / C boundaries.
-constexpr uint32_t CT8 = 32;   // tokens per thread
+constexpr uint32_t CT8 = 16;   // tokens per thread
+constexpr uint32_t CU8 = 8;    // rows loaded together (independent loads in flight per thread)
 __global__ void __launch_bounds__(128) k_conv4_silu_split8(const __half* __restrict__ xbc, uint64_t in_stride,
                                                            const __half* __restrict__ w,
                                                            const __half* __restrict__ bias, __half* __restrict__ xo,
@@ -112,25 +113,34 @@ __global__ void __launch_bounds__(128) k_conv4_silu_split8(const __half* __restr
     else if (d0 < d_inner + GN) { dst = bo + (d0 - d_inner); ds = GN; }
     else { dst = co + (d0 - d_inner - GN); ds = GN; }
     const uint32_t tend = min(t0 + CT8, L);
-    for (uint32_t t = t0; t < tend; ++t) {
-        const uint4 u = *reinterpret_cast<const uint4*>(xb + (uint64_t)t * in_stride);
-        const __half* h = reinterpret_cast<const __half*>(&u);
-        uint4 o;
-        __half* oh = reinterpret_cast<__half*>(&o);
+    for (uint32_t tc = t0; tc < tend; tc += CU8) {
+        // the rows of CU8 tokens are loaded before any is used: the loads are in flight together
+        uint4 rows[CU8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float xn = __half2float(h[e]);
-            float acc = bv[e];
-            acc += wk[e][0] * win[0][e];
-            acc += wk[e][1] * win[1][e];
-            acc += wk[e][2] * win[2][e];
-            acc += wk[e][3] * xn;
-            oh[e] = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
-            win[0][e] = win[1][e];
-            win[1][e] = win[2][e];
-            win[2][e] = xn;
+        for (uint32_t i = 0; i < CU8; ++i)
+            rows[i] = tc + i < tend ? *reinterpret_cast<const uint4*>(xb + (uint64_t)(tc + i) * in_stride)
+                                    : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (uint32_t i = 0; i < CU8; ++i) {
+            if (tc + i >= tend) break;
+            const __half* h = reinterpret_cast<const __half*>(&rows[i]);
+            uint4 o;
+            __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float xn = __half2float(h[e]);
+                float acc = bv[e];
+                acc += wk[e][0] * win[0][e];
+                acc += wk[e][1] * win[1][e];
+                acc += wk[e][2] * win[2][e];
+                acc += wk[e][3] * xn;
+                oh[e] = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
+                win[0][e] = win[1][e];
+                win[1][e] = win[2][e];
+                win[2][e] = xn;
+            }
+            *reinterpret_cast<uint4*>(dst + ((uint64_t)b * L + tc + i) * ds) = o;
         }
-        *reinterpret_cast<uint4*>(dst + ((uint64_t)b * L + t) * ds) = o;
     }
 }
 

@@ -329,20 +329,26 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
                                          static_cast<__half*>(y), M, N, K, epilogue);
         return cudaGetLastError();
     }
-    // Choose the N tile that wastes the fewest SM-slots over the persistent waves.
+    // N tile: the share of SM-slots the persistent waves fill, times a shared-memory factor. At
+    // M = 128 one K = 16 MMA reads 4 KB of A and 32 * BN bytes of B in ~0.52 * BN cycles, so
+    // narrow tiles need more operand bytes per cycle than shared memory sustains (~100 of the
+    // nominal 128 B / cycle): 128 -> 123, 160 -> 111, 192 -> 102, 256 -> 92 B / cycle.
     const int sms = sm_count();
     const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
     double best = -1.0;
     int best_bn = 256;
-    const int cands[3] = {256, 192, 128};
+    const int cands[4] = {256, 192, 160, 128};
     for (int c : cands) {
         const uint32_t tiles = mt * ((N + c - 1) / c);
         const uint32_t waves = (tiles + sms - 1) / sms;
         const double eff = (double)M * N / ((double)waves * sms * GEMM_BM * c);
-        if (eff > best + 1e-9) { best = eff; best_bn = c; }
+        const double bpc = (4096.0 + 32.0 * c) / (0.52 * c);
+        const double score = eff * (bpc > 100.0 ? 100.0 / bpc : 1.0);
+        if (score > best + 1e-9) { best = score; best_bn = c; }
     }
     if (best_bn == 256) return run_gemm_tc<256>(x, w, y, M, N, K, epilogue, sms, s);
     if (best_bn == 192) return run_gemm_tc<192>(x, w, y, M, N, K, epilogue, sms, s);
+    if (best_bn == 160) return run_gemm_tc<160>(x, w, y, M, N, K, epilogue, sms, s);
     return run_gemm_tc<128>(x, w, y, M, N, K, epilogue, sms, s);
 }
 

@@ -58,7 +58,9 @@ def test_backend_loaded_and_registry():
     assert lssm.lib().lssm_has_kernel(b"ssd_chunked_f16") == 1
 
 
-@pytest.mark.parametrize("rows,dim", [(3, 2560), (5, 12), (1, 768)])
+# 16-byte path (dim % 8 == 0, row in registers, up to 1024 octets): 2560, 768, 5120, 8192, 16;
+# element path: 12, 8200 (1025 octets).
+@pytest.mark.parametrize("rows,dim", [(3, 2560), (5, 12), (1, 768), (2, 5120), (4, 8192), (2, 8200), (3, 16)])
 def test_rmsnorm(ctx, ops, rows, dim):
     x = h(RNG.standard_normal((rows, dim)) * 3)
     w = h(RNG.uniform(0.5, 1.5, dim))
