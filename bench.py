@@ -815,7 +815,9 @@ def run_tp8b(args, world, rank, local, dist, ctx=None, steps=None, warmup=None, 
             "config": {"workload": f"8B-shape: batch {B}, prefill {plen} + {steps_new} greedy decode tokens",
                        "model": "mamba2-8b-shape (56L, d_model 4096, 128x64 heads, 8 groups, d_state 128, vocab 256000)",
                        "global_batch": B, "seq_len": plen,
-                       "parallelism": f"heads tensor-parallel x{world} (NCCL all-reduce after out_proj)" if world > 1
+                       "parallelism": (f"heads tensor-parallel x{world} (decode all-reduces by peer-memory exchange "
+                                       "over NVLink when every rank has its own GPU, else NCCL; prefill NCCL)")
+                       if world > 1
                        else "one GPU, unsharded",
                        "l2": f"no flush: each decode step streams {step_bytes / 1e9:.2f} GB per GPU (> 126 MB L2)"},
             "prefill_tok_s": prefill_tok_s,
