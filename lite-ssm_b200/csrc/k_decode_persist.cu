@@ -8,7 +8,7 @@
 // Why one kernel: a batch-1 decode token streams 2.05 GB of weights and state in
 // ~0.32 ms at HBM speed, while a kernel-per-op step has ~260 launches whose ramp-up,
 // tail and launch gaps cost several times that. Here:
-//   * warp 7 is the TMA producer: it walks this CTA's weight chunks for every layer
+//   * warp 10 is the TMA producer: it walks this CTA's weight chunks for every layer
 //     and token in order and streams each chunk (16 rows x seg * 128 bytes, plus the
 //     INT4 scales) with ONE tensor-map copy (128-byte swizzle, L2 evict-first) into
 //     an 11-stage shared-memory ring, and bulk-copies this CTA's rows of the layer's
@@ -62,9 +62,12 @@ namespace {
 
 // 10 consumer warps + 1 producer warp (352 threads). With 3 warps on some SM sub-partitions
 // (16384 registers each) a thread may use at most 168 registers. An INT4 ring
-// stage holds 16 rows x 5 segments of 256 k; consumer warp w reads half of segment w / 2
-// (four 32-wide blocks), so the 10 warps split every stage evenly.
+// stage holds 16 rows x 5 segments of 256 k. The consumer warps form two halves that take
+// alternate ring stages; warp w of a half reads segment w of a stage (eight 32-wide blocks),
+// so one half releases each stage and two stages are consumed at a time.
 constexpr int CONS_WARPS = 10, CONS = CONS_WARPS * 32, THREADS = CONS + 32;
+constexpr uint32_t HALF_WARPS = CONS_WARPS / 2;
+static_assert(HALF_WARPS == 5, "one consumer warp per segment of a stage");
 constexpr int RING = 11;
 constexpr uint32_t STAGE = 12288;                         // 1024-aligned (128-byte swizzle atoms)
 constexpr uint32_t NOCT = 2;                              // staged octets (or residual quads) per thread
@@ -222,12 +225,27 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
     return line * 128 + ((j ^ (line & 7)) << 4);
 }
 
-// INT4 chunk (16 rows x seg*256 k) in column mode: warp w takes half h = w & 1 of
-// segment s = w >> 1 (four 32-wide blocks); warps beyond 2 * seg have no work in the stage.
+// Two k16 MMAs of one 32-wide block j of a segment line (rows g and g + 8), the B fragment
+// (bx, by | bz, bw) supplied by the caller.
+__device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint32_t off, uint32_t bx, uint32_t by,
+                                          uint32_t bz, uint32_t bw, float da[4], float db[4]) {
+    const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
+    const uint32_t wb = *reinterpret_cast<const uint32_t*>(ra + rb8 + off);
+    uint32_t qa[4], qb[4];
+    dequant_word_fold(wa, qa);
+    dequant_word_fold(wb, qb);
+    const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
+    const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
+    mma_16816(da, a1, bx, by);
+    mma_16816(db, a2, bz, bw);
+}
+
+// INT4 chunk (16 rows x seg*256 k) in column mode: warp w of a consumer half takes the
+// whole segment s = w % HALF_WARPS (eight 32-wide blocks); warps s >= seg have no work.
 // Each of the MMA's 8 columns carries one (block, sequence) pair: with one sequence,
-// column j is block 8s + j (this half uses columns 4h..4h+3); with two, column 2j + m is
-// block 8s + 4h + j of sequence m. Only the lanes of a column's group supply that block's
-// activation fragment (the others zero), so after the four blocks column n holds
+// column j is block 8s + j; with two, the segment runs as two passes h of four blocks and
+// column 2j + m is block 8s + 4h + j of sequence m. Only the lanes of a column's group
+// supply that block's activation fragment (the others zero), so column n ends up holding
 // sum_k W[row][k] x_n[k] of its block alone and the scales are applied once per column.
 // The weights use the bias-folded dequantisation (exact fp16 values 72 + q); the folded
 // 72 * sum(x) of each block is cancelled by starting the accumulator at -72 * xsum.
@@ -235,74 +253,73 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
                                              const float* xsum, uint32_t K8, uint32_t K32, uint32_t M,
                                              float acc[4]) {
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t sgi = warp >> 1, h = warp & 1;
+    const uint32_t lane = threadIdx.x & 31, sgi = (threadIdx.x >> 5) % HALF_WARPS;
     if (sgi >= seg) return;
     const uint32_t g = lane >> 2, c = lane & 3;
     const uint32_t rowb = seg * 128;
     const uint32_t line = g * seg + sgi;                 // 128-byte line of row g, segment sgi
-    const uint32_t hp = ((4 * h) ^ (line & 7)) << 4;     // swizzled 16-byte chunk of block 4h (rows g, g + 8)
+    const uint32_t sw = line & 7;                        // swizzle of the line's 16-byte chunks (one per block)
     const uint8_t* ra = stage + line * 128 + 4 * c;
     const uint32_t rb8 = 8 * rowb;
     const uint32_t blk0 = chunk * seg * 8 + sgi * 8;     // first block of the segment (whole-K index)
     const __half* sc = reinterpret_cast<const __half*>(stage + 16 * rowb) + g * seg * 8 + sgi * 8;
-    // this lane's column: block (within the half) and sequence
-    const bool one = M == 1;
-    const uint32_t myj = one ? (g & 3) : (g >> 1), mym = one ? 0 : (g & 1);
-    const bool act = one ? ((g >> 2) == h) : true;
-    const uint4 xg = act ? xs[(uint64_t)mym * K8 + (uint64_t)(blk0 + 4 * h + myj) * 4 + c] : make_uint4(0, 0, 0, 0);
-    // accumulator start: -72 * block sum of the lane's two columns (rows g and g + 8 share them)
-    float i0, i1;
-    if (one) {   // columns 2c, 2c + 1 = blocks 2c, 2c + 1 of the segment; live in half c >> 1
-        const bool live = (c >> 1) == h;
+    if (M == 1) {
+        // column g = block g; the lane's accumulator columns 2c, 2c + 1 = blocks 2c, 2c + 1
+        const uint4 xg = xs[(uint64_t)(blk0 + g) * 4 + c];
         const float2 xsv = *reinterpret_cast<const float2*>(xsum + blk0 + 2 * c);
-        i0 = live ? -72.0f * xsv.x : 0.0f;
-        i1 = live ? -72.0f * xsv.y : 0.0f;
-    } else {     // columns 2c, 2c + 1 = block 4h + c of sequences 0, 1
-        i0 = -72.0f * xsum[blk0 + 4 * h + c];
-        i1 = -72.0f * xsum[K32 + blk0 + 4 * h + c];
-    }
-    float da[4] = {i0, i1, i0, i1}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float i0 = -72.0f * xsv.x, i1 = -72.0f * xsv.y;
+        // column 2c (an even block) accumulates in da / db, column 2c + 1 in ea / eb
+        float da[4] = {i0, 0.0f, i0, 0.0f}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float ea[4] = {0.0f, i1, 0.0f, i1}, eb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (uint32_t j = 0; j < 4; ++j) {
-        const uint32_t off = hp ^ (j << 4);
-        const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
-        const uint32_t wb = *reinterpret_cast<const uint32_t*>(ra + rb8 + off);
-        uint32_t qa[4], qb[4];
-        dequant_word_fold(wa, qa);
-        dequant_word_fold(wb, qb);
-        const bool mine = myj == j;
-        const uint32_t bx = mine ? xg.x : 0u, by = mine ? xg.y : 0u, bz = mine ? xg.z : 0u, bw = mine ? xg.w : 0u;
-        const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
-        const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
-        mma_16816(da, a1, bx, by);
-        mma_16816(db, a2, bz, bw);
-    }
-    const float d0 = da[0] + db[0], d1 = da[1] + db[1], d2 = da[2] + db[2], d3 = da[3] + db[3];
-    if (one) {
+        for (uint32_t j = 0; j < 8; ++j) {
+            const bool mine = g == j;
+            const uint32_t bx = mine ? xg.x : 0u, by = mine ? xg.y : 0u, bz = mine ? xg.z : 0u, bw = mine ? xg.w : 0u;
+            // even and odd blocks accumulate into separate pairs: two chains of four MMAs each
+            if (j & 1) mma_block(ra, rb8, (j ^ sw) << 4, bx, by, bz, bw, ea, eb);
+            else mma_block(ra, rb8, (j ^ sw) << 4, bx, by, bz, bw, da, db);
+        }
+        const float d0 = (da[0] + db[0]) + (ea[0] + eb[0]), d1 = (da[1] + db[1]) + (ea[1] + eb[1]);
+        const float d2 = (da[2] + db[2]) + (ea[2] + eb[2]), d3 = (da[3] + db[3]) + (ea[3] + eb[3]);
         const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(sc + 2 * c));
         const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(sc + 8 * seg * 8 + 2 * c));
         acc[0] += d0 * sa.x + d1 * sa.y;
         acc[2] += d2 * sb.x + d3 * sb.y;
-    } else {
+        return;
+    }
+    // two sequences: lane column (block myj of the pass, sequence mym)
+    const uint32_t myj = g >> 1, mym = g & 1;
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+        const uint4 xg = xs[(uint64_t)mym * K8 + (uint64_t)(blk0 + 4 * h + myj) * 4 + c];
+        // accumulator start: -72 * block sum of the lane's columns 2c, 2c + 1 = block 4h + c of sequences 0, 1
+        const float i0 = -72.0f * xsum[blk0 + 4 * h + c], i1 = -72.0f * xsum[K32 + blk0 + 4 * h + c];
+        float da[4] = {i0, i1, i0, i1}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const bool mine = myj == j;
+            const uint32_t bx = mine ? xg.x : 0u, by = mine ? xg.y : 0u, bz = mine ? xg.z : 0u, bw = mine ? xg.w : 0u;
+            mma_block(ra, rb8, ((4 * h + j) ^ sw) << 4, bx, by, bz, bw, da, db);
+        }
         const float sa = __half2float(sc[4 * h + c]), sb = __half2float(sc[8 * seg * 8 + 4 * h + c]);
-        acc[0] += d0 * sa;
-        acc[1] += d1 * sa;
-        acc[2] += d2 * sb;
-        acc[3] += d3 * sb;
+        acc[0] += (da[0] + db[0]) * sa;
+        acc[1] += (da[1] + db[1]) * sa;
+        acc[2] += (da[2] + db[2]) * sb;
+        acc[3] += (da[3] + db[3]) * sb;
     }
 }
 
-// fp16 chunk (lm_head, 16 rows x seg*64 k): this warp's share of the 16-wide k steps.
+// fp16 chunk (lm_head, 16 rows x seg*64 k): this warp's share (within its consumer half) of
+// the 16-wide k steps.
 __device__ __forceinline__ void consume_f16(const uint8_t* stage, uint32_t seg, uint32_t chunk, const __half* xh,
                                             uint32_t K, uint32_t M, float acc[4]) {
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31, warp = (threadIdx.x >> 5) % HALF_WARPS;
     const uint32_t g = lane >> 2, c = lane & 3;
     const uint32_t nks = seg * 4;
     const bool has_x = g < M;
     const __half* xr = xh + (uint64_t)(has_x ? g : 0) * K + (uint64_t)chunk * seg * 64;
-    const uint32_t k0 = (nks * warp) / CONS_WARPS, k1 = (nks * (warp + 1)) / CONS_WARPS;
-    constexpr uint32_t MAXK = (SEG_MAX * 4 + CONS_WARPS - 1) / CONS_WARPS;
+    const uint32_t k0 = (nks * warp) / HALF_WARPS, k1 = (nks * (warp + 1)) / HALF_WARPS;
+    constexpr uint32_t MAXK = (SEG_MAX * 4 + HALF_WARPS - 1) / HALF_WARPS;
 #pragma unroll
     for (uint32_t i = 0; i < MAXK; ++i) {
         // predicated like consume_int4: past-the-end steps re-read step k0 with a zero activation
@@ -609,7 +626,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     if (tid == 0) {
         for (int s = 0; s < RING; ++s) {
             mbar_init1(smem_u32(&full[s]), 1);
-            mbar_init1(smem_u32(&empty[s]), CONS_WARPS);
+            mbar_init1(smem_u32(&empty[s]), HALF_WARPS);
         }
         mbar_init1(smem_u32(sfull), 1);
         mbar_init1(smem_u32(sempty), 1);
@@ -737,12 +754,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     // ---------------------------------------------------------------- consumers
     uint32_t slot = 0, phase = 0, gen = 0, sphase = 0;
+    uint32_t sn = 0;                       // ring stages passed (all consumers alike)
+    const uint32_t half = warp / HALF_WARPS;   // this warp consumes the stages sn with sn % 2 == half
     uint64_t wait_ns = 0;   // trace: warp 0's time blocked on the ring in this layer
 
     // Consume `nt` (<= TG) units of this CTA starting at unit ordinal i0: units are
     // (tile, chunk) pairs when `split` (one chunk each), else whole tiles of `nch`
-    // chunks. Accumulated per unit in registers; every warp's partial sums then go to
-    // shared memory (readable after the closing barrier).
+    // chunks. Each stage is consumed by one half of the warps (alternating); accumulated
+    // per unit in registers; every warp's partial sums (zero for units it had no stage of)
+    // then go to shared memory (readable after the closing barrier).
     auto consume_group = [&](bool int4, uint32_t seg, uint32_t nch, uint32_t K, bool split, uint32_t i0,
                              uint32_t nt) -> bool {
         float acc[TG][4];
@@ -754,16 +774,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 const uint32_t u = cta + (i0 + ti) * G;
                 const uint32_t c0 = split ? u % nch : 0, c1 = split ? c0 + 1 : nch;
                 for (uint32_t c = c0; c < c1; ++c) {
-                    const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
-                    if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) { bad = true; break; }
-                    if (p.trace && tid == 0) wait_ns += gtimer() - w0;
-                    const uint8_t* stage = smem + OFF_RING + slot * STAGE;
-                    if (int4)
-                        consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32, NB,
-                                     acc[ti]);
-                    else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, NB, acc[ti]);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
+                    if ((sn & 1) == half) {
+                        const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
+                        if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) { bad = true; break; }
+                        if (p.trace && tid == 0) wait_ns += gtimer() - w0;
+                        const uint8_t* stage = smem + OFF_RING + slot * STAGE;
+                        if (int4)
+                            consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32,
+                                         NB, acc[ti]);
+                        else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, NB, acc[ti]);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
+                    }
+                    ++sn;
                     if (++slot == RING) { slot = 0; phase ^= 1; }
                 }
             }
