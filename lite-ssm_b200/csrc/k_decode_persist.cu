@@ -75,7 +75,7 @@ constexpr uint32_t SEG_MAX = 5;                           // 16 x 5 x 128 B + IN
 constexpr uint32_t TG = 5;                                // tiles per register-accumulated group
 constexpr uint32_t XBUF = 20480;                          // staged activation (<= 2 x 5120 halves)
 constexpr uint32_t PART = TG * CONS_WARPS * 8 * 4 * 4;    // per-warp partial sums of one group ([ti][warp][g][4])
-constexpr uint32_t XSUM = 2 * 5120 / 32 * 4;              // per-block sums of the staged activation (fp32)
+constexpr uint32_t XSUM = 2 * 5120 / 32 * 8;              // per-block {even, odd} sums of the staged activation
 constexpr uint32_t SBUF = 40960;                          // this CTA's ssd state rows (<= 80 x 128 fp32)
 constexpr uint32_t SROWS = SBUF / 512;
 constexpr uint32_t HBUF = 10240;                          // hidden vector(s) (B x d_model fp16)
@@ -225,6 +225,24 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
     return line * 128 + ((j ^ (line & 7)) << 4);
 }
 
+// Bias-folding dequantisation of one packed word (nibbles u = q + 8 of k0..k7, q signed) into
+// the MMA pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), with one shift: the even nibbles k0 / k4 and
+// (after w >> 8) k2 / k6 sit in bits 0..3 of their fp16 lanes and are written under the
+// exponent of 1024 (unit 1 there), the odd ones sit in bits 4..7 and are written under the
+// exponent of 64 (unit 1 there). The values are exact: 1032 + q for even k, 72 + q for odd
+// k, so a block's dot product with x equals sum(q * x) + 1032 * sum(x_even) + 72 * sum(x_odd)
+// and the caller starts the accumulator at minus that bias. 5 instructions per word.
+__device__ __forceinline__ void dequant_word_fold2(uint32_t w, uint32_t q[4]) {
+    const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, M1024 = 0x64086408u, M64 = 0x54805480u;
+    const uint32_t w8 = w >> 8;
+    q[0] = lop3_6a(w, LO, M1024);
+    q[1] = lop3_6a(w, HI, M64);
+    q[2] = lop3_6a(w8, LO, M1024);
+    q[3] = lop3_6a(w8, HI, M64);
+}
+// Accumulator start of a block from its {even, odd} activation sums.
+__device__ __forceinline__ float fold_bias(float2 s) { return fmaf(-1032.0f, s.x, -72.0f * s.y); }
+
 // Two k16 MMAs of one 32-wide block j of a segment line (rows g and g + 8), the B fragment
 // (bx, by | bz, bw) supplied by the caller.
 __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint32_t off, uint32_t bx, uint32_t by,
@@ -232,8 +250,8 @@ __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint3
     const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
     const uint32_t wb = *reinterpret_cast<const uint32_t*>(ra + rb8 + off);
     uint32_t qa[4], qb[4];
-    dequant_word_fold(wa, qa);
-    dequant_word_fold(wb, qb);
+    dequant_word_fold2(wa, qa);
+    dequant_word_fold2(wb, qb);
     const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
     const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
     mma_16816(da, a1, bx, by);
@@ -247,8 +265,8 @@ __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint3
 // column 2j + m is block 8s + 4h + j of sequence m. Only the lanes of a column's group
 // supply that block's activation fragment (the others zero), so column n ends up holding
 // sum_k W[row][k] x_n[k] of its block alone and the scales are applied once per column.
-// The weights use the bias-folded dequantisation (exact fp16 values 72 + q); the folded
-// 72 * sum(x) of each block is cancelled by starting the accumulator at -72 * xsum.
+// The weights use the bias-folded dequantisation (dequant_word_fold2); the folded bias of each
+// block is cancelled by starting the accumulator at fold_bias of its activation sums.
 // acc: rows g / g + 8 (one sequence: acc[0] / acc[2]; two: acc[0..1] / acc[2..3] per m).
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
                                              const float* xsum, uint32_t K8, uint32_t K32, uint32_t M,
@@ -266,8 +284,8 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
     if (M == 1) {
         // column g = block g; the lane's accumulator columns 2c, 2c + 1 = blocks 2c, 2c + 1
         const uint4 xg = xs[(uint64_t)(blk0 + g) * 4 + c];
-        const float2 xsv = *reinterpret_cast<const float2*>(xsum + blk0 + 2 * c);
-        const float i0 = -72.0f * xsv.x, i1 = -72.0f * xsv.y;
+        const float4 xsv = *reinterpret_cast<const float4*>(xsum + 2 * (blk0 + 2 * c));
+        const float i0 = fold_bias(make_float2(xsv.x, xsv.y)), i1 = fold_bias(make_float2(xsv.z, xsv.w));
         // column 2c (an even block) accumulates in da / db, column 2c + 1 in ea / eb
         float da[4] = {i0, 0.0f, i0, 0.0f}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         float ea[4] = {0.0f, i1, 0.0f, i1}, eb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -292,8 +310,9 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
 #pragma unroll
     for (uint32_t h = 0; h < 2; ++h) {
         const uint4 xg = xs[(uint64_t)mym * K8 + (uint64_t)(blk0 + 4 * h + myj) * 4 + c];
-        // accumulator start: -72 * block sum of the lane's columns 2c, 2c + 1 = block 4h + c of sequences 0, 1
-        const float i0 = -72.0f * xsum[blk0 + 4 * h + c], i1 = -72.0f * xsum[K32 + blk0 + 4 * h + c];
+        // accumulator start: the folded bias of the lane's columns 2c, 2c + 1 = block 4h + c of sequences 0, 1
+        const float2* xs2 = reinterpret_cast<const float2*>(xsum);
+        const float i0 = fold_bias(xs2[blk0 + 4 * h + c]), i1 = fold_bias(xs2[K32 + blk0 + 4 * h + c]);
         float da[4] = {i0, i1, i0, i1}, db[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
@@ -339,12 +358,13 @@ __device__ __forceinline__ void consume_f16(const uint8_t* stage, uint32_t seg, 
 
 // One staged octet q of sequence m: half(x * w * rr) (rmsnorm_f16 arithmetic) -> xbuf, in
 // the INT4 MMA fragment order {x0,x4} {x1,x5} {x2,x6} {x3,x7} when frag; with frag also the
-// fp32 sum of its 32-wide block's staged values -> xsum[m][q / 4] (the four octets of a block
-// belong to four consecutive threads: a quad shuffle). Every consumer thread calls it;
-// `valid` = q < nq (uniform over each quad, as nq % 4 == 0).
+// fp32 sums of its 32-wide block's staged values at even and at odd positions within the
+// octets -> xsum[m][q / 4] = {even, odd} (the four octets of a block belong to four
+// consecutive threads: a quad shuffle). Every consumer thread calls it; `valid` = q < nq
+// (uniform over each quad, as nq % 4 == 0).
 __device__ __forceinline__ void stage_octet(uint4 xv, uint4 wv, float rr, bool frag, bool valid, uint32_t m,
                                             uint32_t q, uint32_t nq, uint8_t* xbuf, float* xsum) {
-    float s8 = 0.0f;
+    float se = 0.0f, so = 0.0f;
     if (valid) {
         const __half* xh8 = reinterpret_cast<const __half*>(&xv);
         const __half* wh8 = reinterpret_cast<const __half*>(&wv);
@@ -360,16 +380,22 @@ __device__ __forceinline__ void stage_octet(uint4 xv, uint4 wv, float rr, bool f
             u.z = *reinterpret_cast<uint32_t*>(&o2);
             u.w = *reinterpret_cast<uint32_t*>(&o3);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) s8 += __half2float(v[j]);
+            for (int j = 0; j < 8; j += 2) {
+                se += __half2float(v[j]);
+                so += __half2float(v[j + 1]);
+            }
         } else {
             u = *reinterpret_cast<uint4*>(v);
         }
         reinterpret_cast<uint4*>(xbuf)[(uint64_t)m * nq + q] = u;
     }
     if (frag) {
-        s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
-        s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
-        if (valid && (q & 3) == 0) xsum[m * (nq >> 2) + (q >> 2)] = s8;
+        se += __shfl_xor_sync(0xffffffffu, se, 1);
+        so += __shfl_xor_sync(0xffffffffu, so, 1);
+        se += __shfl_xor_sync(0xffffffffu, se, 2);
+        so += __shfl_xor_sync(0xffffffffu, so, 2);
+        if (valid && (q & 3) == 0)
+            reinterpret_cast<float2*>(xsum)[m * (nq >> 2) + (q >> 2)] = make_float2(se, so);
     }
 }
 
