@@ -95,7 +95,8 @@ constexpr uint32_t OFF_LT = OFF_RSLOT + 128;              // layer table
 constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[32], tok[2], abort, slots, arg v[32] / i[32]
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 512;
+constexpr uint32_t OFF_ZERO = OFF_MISC + 512;             // 16 zero bytes (masked MMA fragments)
+constexpr uint32_t SMEM_BYTES = OFF_ZERO + 16;
 constexpr uint64_t SPIN_NS = 2000000000ull;
 static_assert(SMEM_BYTES <= 232448, "persistent decode kernel exceeds 227 KB of shared memory");
 static_assert(sizeof(PLayer) % 8 == 0 && OFF_BAR % 8 == 0, "layer table / barriers misaligned");
@@ -270,7 +271,7 @@ __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint3
 // acc: rows g / g + 8 (one sequence: acc[0] / acc[2]; two: acc[0..1] / acc[2..3] per m).
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,
                                              const float* xsum, uint32_t K8, uint32_t K32, uint32_t M,
-                                             float acc[4]) {
+                                             uint32_t zaddr, float acc[4]) {
     const uint32_t lane = threadIdx.x & 31, sgi = (threadIdx.x >> 5) % HALF_WARPS;
     if (sgi >= seg) return;
     const uint32_t g = lane >> 2, c = lane & 3;
@@ -282,8 +283,10 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
     const uint32_t blk0 = chunk * seg * 8 + sgi * 8;     // first block of the segment (whole-K index)
     const __half* sc = reinterpret_cast<const __half*>(stage + 16 * rowb) + g * seg * 8 + sgi * 8;
     if (M == 1) {
-        // column g = block g; the lane's accumulator columns 2c, 2c + 1 = blocks 2c, 2c + 1
-        const uint4 xg = xs[(uint64_t)(blk0 + g) * 4 + c];
+        // column g = block g; the lane's accumulator columns 2c, 2c + 1 = blocks 2c, 2c + 1.
+        // The B fragment of block j is this lane's activation quad when g == j, else 16 zero
+        // bytes: one shared load from a selected address (no per-register masking).
+        const uint32_t xa = smem_u32(xs + (blk0 + g) * 4 + c);
         const float4 xsv = *reinterpret_cast<const float4*>(xsum + 2 * (blk0 + 2 * c));
         const float i0 = fold_bias(make_float2(xsv.x, xsv.y)), i1 = fold_bias(make_float2(xsv.z, xsv.w));
         // column 2c (an even block) accumulates in da / db, column 2c + 1 in ea / eb
@@ -291,8 +294,10 @@ __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg,
         float ea[4] = {0.0f, i1, 0.0f, i1}, eb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (uint32_t j = 0; j < 8; ++j) {
-            const bool mine = g == j;
-            const uint32_t bx = mine ? xg.x : 0u, by = mine ? xg.y : 0u, bz = mine ? xg.z : 0u, bw = mine ? xg.w : 0u;
+            uint32_t bx, by, bz, bw;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(bx), "=r"(by), "=r"(bz), "=r"(bw)
+                         : "r"(g == j ? xa : zaddr));
             // even and odd blocks accumulate into separate pairs: two chains of four MMAs each
             if (j & 1) mma_block(ra, rb8, (j ^ sw) << 4, bx, by, bz, bw, ea, eb);
             else mma_block(ra, rb8, (j ^ sw) << 4, bx, by, bz, bw, da, db);
@@ -656,6 +661,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         }
         mbar_init1(smem_u32(sfull), 1);
         mbar_init1(smem_u32(sempty), 1);
+        *reinterpret_cast<uint4*>(smem + OFF_ZERO) = make_uint4(0, 0, 0, 0);
         *abort = 0;
         // distinct (seq, group) pairs of this CTA's state rows -> B / C slots
         uint32_t ns = 0;
@@ -807,7 +813,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         const uint8_t* stage = smem + OFF_RING + slot * STAGE;
                         if (int4)
                             consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32,
-                                         NB, acc[ti]);
+                                         NB, smem_u32(smem + OFF_ZERO), acc[ti]);
                         else consume_f16(stage, seg, c, reinterpret_cast<const __half*>(xbuf), K, NB, acc[ti]);
                         __syncwarp();
                         if (lane == 0) mbar_arrive1(smem_u32(&empty[slot]));
