@@ -552,24 +552,58 @@ __device__ void stage_norm_h(const float* opart, uint32_t nch, const uint32_t* t
 }
 
 // In_proj work of CTA s (owner computes): channel units of 8 d_inner channels are dealt in
-// contiguous ranges, the first `extra` CTAs taking one more; the z rows and x rows of a unit
-// form one 16-row tile (two 8-row halves), so the CTA that runs the ssd rows of a channel
-// also computes its x and z. The "special" tiles hold the B, C and dt rows (16 rows at
-// 2 d_inner + 16 k); special tile k goes to CTA (extra + k) mod G, i.e. first to CTAs with
-// fewer units, and each CTA runs its special tiles before its units, so the rows every CTA
-// polls are written early.
+// contiguous ranges; the z rows and x rows of a unit form one 16-row tile (two 8-row
+// halves), so the CTA that runs the ssd rows of a channel also computes its x and z. The
+// "special" tiles hold the B, C and dt rows (16 rows at 2 d_inner + 16 k); each CTA runs
+// its special tiles first, as a group of their own, so the rows every CTA polls are written
+// early. That extra group costs about one more tile, so a CTA with a special tile is
+// charged two units: with T = ceil((units + 2 * special tiles) / G), special tile k goes to
+// CTA k, which takes T - 2 units, the other CTAs take T, and the last E CTAs one fewer
+// (E = G * T - 2 * special - units). Shapes where that does not fit (more special tiles
+// than CTAs, T < 2, or the reduced CTAs reaching the special ones) deal the units evenly
+// (the first NU % G CTAs one more) and the special tiles to CTAs with fewer units.
 struct InTiles {
     uint32_t ub, nu;      // first unit, units
     uint32_t kfirst, nsp; // first special tile index, special tiles (k = kfirst + i * G)
 };
+struct InPlan {
+    uint32_t T, E;
+    bool fold;            // special tiles charged as two units (else the even deal)
+};
+__host__ __device__ __forceinline__ InPlan in_plan(uint32_t G, uint32_t di, uint32_t nspec) {
+    const uint32_t NU = di / 8;
+    InPlan q;
+    q.T = (NU + 2 * nspec + G - 1) / G;
+    q.E = G * q.T - 2 * nspec - NU;
+    q.fold = nspec <= G && nspec + q.E <= G && q.T >= 2;
+    return q;
+}
 __host__ __device__ __forceinline__ InTiles in_tiles(uint32_t s, uint32_t G, uint32_t di, uint32_t nspec) {
-    const uint32_t NU = di / 8, base = NU / G, extra = NU % G;
+    const InPlan q = in_plan(G, di, nspec);
     InTiles t;
+    if (q.fold) {
+        const uint32_t cut = G - q.E;   // CTAs >= cut take one unit fewer
+        t.nsp = s < nspec ? 1u : 0u;
+        t.kfirst = s;
+        t.nu = q.T - 2 * t.nsp - (s >= cut ? 1u : 0u);
+        t.ub = s * q.T - 2 * (s < nspec ? s : nspec) - (s > cut ? s - cut : 0u);
+        return t;
+    }
+    const uint32_t NU = di / 8, base = NU / G, extra = NU % G;
     t.nu = base + (s < extra ? 1u : 0u);
     t.ub = s * base + (s < extra ? s : extra);
     t.kfirst = (s + G - (extra % G)) % G;
     t.nsp = t.kfirst < nspec ? (nspec - 1 - t.kfirst) / G + 1 : 0;
     return t;
+}
+// Upper bounds over the CTAs of units and of in_proj tiles (special + units) per CTA.
+__host__ __device__ __forceinline__ uint32_t in_max_units(uint32_t G, uint32_t di, uint32_t nspec) {
+    const InPlan q = in_plan(G, di, nspec);
+    return q.fold ? q.T : (di / 8 + G - 1) / G;
+}
+__host__ __device__ __forceinline__ uint32_t in_max_tiles(uint32_t G, uint32_t di, uint32_t nspec) {
+    const InPlan q = in_plan(G, di, nspec);
+    return q.fold ? q.T : (di / 8 + G - 1) / G + (nspec + G - 1) / G;
 }
 // Row starts of the two 8-row halves of tile ti of a CTA.
 __device__ __forceinline__ void in_tile_rows(const InTiles& t, uint32_t ti, uint32_t G, uint32_t di, uint32_t& h0,
@@ -644,12 +678,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
     if (p.dconv > 4 || p.dconv < 1 || NB > 2 || NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
-        NB * 8 * ((p.di / 8 + G - 1) / G) > SROWS || p.di % 8 || p.H * p.P != p.di ||
+        NB * 8 * in_max_units(G, p.di, nspec) > SROWS || p.di % 8 || p.H * p.P != p.di ||
         p.n_layer > LT_MAX || (uint64_t)NB * max(p.dm, p.di) * 2 > XBUF || (uint64_t)NB * p.dm * 2 > HBUF ||
         p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
         nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
-        p.H % p.G || ((p.di / 8 + G - 1) / G + (nspec + G - 1) / G) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
+        p.H % p.G || in_max_tiles(G, p.di, nspec) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -1196,10 +1230,10 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     if ((uint64_t)sh.B * sh.dm * 2 > HBUF) return "hidden vectors exceed 10 KB";
     if (sh.di % 8 || sh.H * sh.P != sh.di) return "d_inner must be n_heads x d_head, a multiple of 8";
     const uint32_t nspec = (2 * sh.G * sh.N + sh.H + 15) / 16;
-    if (((sh.di / 8 + G - 1) / G + (nspec + G - 1) / G) * 16 * sh.B > CONS) return "too many in_proj rows per SM";
+    if (in_max_tiles(G, sh.di, nspec) * 16 * sh.B > CONS) return "too many in_proj rows per SM";
     if (sh.dm / 4 > NOCT * CONS) return "d_model too wide for the residual pass (<= 2560)";
     if (sh.H % sh.G) return "n_heads not divisible by n_groups";
-    if ((uint64_t)sh.B * 8 * ((sh.di / 8 + G - 1) / G) > SROWS) return "ssd state rows per SM exceed 40 KB";
+    if ((uint64_t)sh.B * 8 * in_max_units(G, sh.di, nspec) > SROWS) return "ssd state rows per SM exceed 40 KB";
     *seg_in = odd_seg(sh.dm / 256);
     *seg_out = odd_seg(sh.di / 256);
     *seg_lm = odd_seg(sh.dm / 64);

@@ -13,6 +13,7 @@ entry point raises.
 
 from __future__ import annotations
 
+import atexit
 import ctypes as C
 import os
 import weakref
@@ -194,6 +195,21 @@ def cuda_available() -> bool:
         return False
 
 
+_LIVE_CTX: "weakref.WeakSet[Ctx]" = weakref.WeakSet()
+
+
+@atexit.register
+def _close_live_contexts():
+    """At interpreter exit, while the library and this module are still whole, close every
+    context that is still open (its sessions, models and buffers first), instead of leaving
+    the native teardown to the order in which module globals happen to be cleared."""
+    for c in list(_LIVE_CTX):
+        try:
+            c.close()
+        except Exception:
+            pass
+
+
 class Ctx:
     """One per host thread (MetalOps' threading model)."""
 
@@ -203,6 +219,7 @@ class Ctx:
         self.h = h
         self.device = device
         self._deps = []   # weak refs to sessions / models / buffers made on this context
+        _LIVE_CTX.add(self)
 
     def _track(self, obj):
         if len(self._deps) > 256:
