@@ -96,7 +96,8 @@ constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[32], tok[2], abort, slots, arg v[32] / i[32]
 constexpr uint32_t OFF_ZERO = OFF_MISC + 512;             // 16 zero bytes (masked MMA fragments)
-constexpr uint32_t SMEM_BYTES = OFF_ZERO + 16;
+constexpr uint32_t OFF_CONV = OFF_ZERO + 16;              // per consumer thread: its conv row's inputs (16 B)
+constexpr uint32_t SMEM_BYTES = OFF_CONV + CONS * 16;
 constexpr uint64_t SPIN_NS = 2000000000ull;
 static_assert(SMEM_BYTES <= 232448, "persistent decode kernel exceeds 227 KB of shared memory");
 static_assert(sizeof(PLayer) % 8 == 0 && OFF_BAR % 8 == 0, "layer table / barriers misaligned");
@@ -940,6 +941,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             // z / dt and, for xBC rows, conv-state roll + conv + SiLU -> exchange words
             stage_norm_h<NB>(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.dm, true, xbuf, xsum,
                          red);
+            // park the conv inputs in this thread's shared-memory slot: no registers held across in_proj
+            if (convA) {
+                const __half2 c01 = __halves2half2(cwh[0], cwh[1]), c23 = __halves2half2(cwh[2], cwh[3]);
+                const __half2 s12 = __halves2half2(csh[1], csh[2]), s3b = __halves2half2(csh[3], cbh);
+                *reinterpret_cast<uint4*>(smem + OFF_CONV + tid * 16) =
+                    make_uint4(*reinterpret_cast<const uint32_t*>(&c01), *reinterpret_cast<const uint32_t*>(&c23),
+                               *reinterpret_cast<const uint32_t*>(&s12), *reinterpret_cast<const uint32_t*>(&s3b));
+            }
             stamp(lb + 1);
             // special tiles form their own group(s), so their rows are published before the units run
             for (uint32_t g0 = 0, nt = 0; g0 < ntA && ok; g0 += nt) {
@@ -949,6 +958,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
                     if (convA) {
                         // conv-state roll + depthwise conv + SiLU (k_conv_update_silu_split arithmetic)
+                        const uint4 cv = *reinterpret_cast<const uint4*>(smem + OFF_CONV + tid * 16);
+                        const __half* cvh = reinterpret_cast<const __half*>(&cv);
+                        const __half cwh[4] = {cvh[0], cvh[1], cvh[2], cvh[3]};
+                        const __half csh[4] = {__ushort_as_half(0), cvh[4], cvh[5], cvh[6]};
+                        const __half cbh = cvh[7];
                         __half* st = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
                         float acc = __half2float(cbh);
 #pragma unroll
