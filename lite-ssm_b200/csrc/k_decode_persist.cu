@@ -96,8 +96,13 @@ constexpr uint32_t OFF_BAR = OFF_LT + LT_MAX * sizeof(PLayer);
 constexpr uint32_t N_BARS = 2 * RING + 2;
 constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;       // red[32], tok[2], abort, slots, arg v[32] / i[32]
 constexpr uint32_t OFF_ZERO = OFF_MISC + 512;             // 16 zero bytes (masked MMA fragments)
-constexpr uint32_t OFF_CONV = OFF_ZERO + 16;              // per consumer thread: its conv row's inputs (16 B)
-constexpr uint32_t SMEM_BYTES = OFF_CONV + CONS * 16;
+// The in_proj epilogue: thread t < EPI_T owns output (tile t / (16 B), row (t / B) % 16, seq t % B).
+constexpr uint32_t EPI_T = 160;
+constexpr uint32_t OFF_CONV = OFF_ZERO + 16;              // per owning thread: its conv row's inputs (16 B)
+constexpr uint32_t OFF_EPI = OFF_CONV + EPI_T * 16;       // per owning thread: packed output mapping
+constexpr uint32_t SMEM_BYTES = OFF_EPI + EPI_T * 4;
+// packed mapping word: in_proj row (bits 0..19) | owns an output | conv row | B / C / dt row | local state row << 24
+constexpr uint32_t EPI_OWN = 1u << 20, EPI_CONV = 1u << 21, EPI_SPEC = 1u << 22;
 constexpr uint64_t SPIN_NS = 2000000000ull;
 static_assert(SMEM_BYTES <= 232448, "persistent decode kernel exceeds 227 KB of shared memory");
 static_assert(sizeof(PLayer) % 8 == 0 && OFF_BAR % 8 == 0, "layer table / barriers misaligned");
@@ -684,7 +689,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
         p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
         nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
-        p.H % p.G || in_max_tiles(G, p.di, nspec) * 16 * NB > CONS || p.dm / 4 > NOCT * CONS) {
+        p.H % p.G || in_max_tiles(G, p.di, nspec) * 16 * NB > EPI_T || p.dm / 4 > NOCT * CONS ||
+        p.proj >= (1u << 20)) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
     }
@@ -901,16 +907,23 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         }
         return true;
     };
-    // Each thread owns one (tile ordinal, row, seq) output of in_proj for the epilogue.
+    // Each thread t < EPI_T owns one (tile ordinal, row, seq) output of in_proj for the
+    // epilogue; its mapping is packed into shared memory once, so no registers carry it
+    // through the layer loop.
     const uint32_t tiA = tid / (16 * NB), rowA = (tid / NB) % 16, mA = tid % NB;
-    const bool ownA = tiA < ntA;
-    uint32_t hA0 = 0, hA1 = 0;
-    if (ownA) in_tile_rows(tt, tiA, G, p.di, hA0, hA1);
-    const uint32_t rA = rowA < 8 ? hA0 + rowA : hA1 + rowA - 8;   // in_proj output row
-    const bool convA = ownA && rA >= p.di && rA < p.di + p.xd;
-    const uint32_t dA = rA - p.di;
-    const bool specA = tiA < tt.nsp;                               // B / C / dt rows: published
-    const uint32_t jA = mA * urows + (tiA - tt.nsp) * 8 + (rowA & 7);   // unit rows: local state row
+    if (tid < EPI_T) {
+        uint32_t w = 0;
+        if (tiA < ntA) {
+            uint32_t hA0, hA1;
+            in_tile_rows(tt, tiA, G, p.di, hA0, hA1);
+            const uint32_t rA = rowA < 8 ? hA0 + rowA : hA1 + rowA - 8;   // in_proj output row
+            w = rA | EPI_OWN;
+            if (rA >= p.di && rA < p.di + p.xd) w |= EPI_CONV;
+            if (tiA < tt.nsp) w |= EPI_SPEC;                               // B / C / dt rows: published
+            else w |= (mA * urows + (tiA - tt.nsp) * 8 + (rowA & 7)) << 24;   // unit rows: local state row
+        }
+        reinterpret_cast<uint32_t*>(smem + OFF_EPI)[tid] = w;
+    }
 
     bool ok = true;
     for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
@@ -929,7 +942,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             __half cwh[4], csh[4], cbh = __ushort_as_half(0);
 #pragma unroll
             for (uint32_t k = 0; k < 4; ++k) cwh[k] = csh[k] = __ushort_as_half(0);
+            const uint32_t ew0 = tid < EPI_T ? reinterpret_cast<const uint32_t*>(smem + OFF_EPI)[tid] : 0u;
+            const bool convA = ew0 & EPI_CONV;
             if (convA) {
+                const uint32_t dA = (ew0 & 0xFFFFFu) - p.di;
                 const __half* wrow = L.conv_w + (uint64_t)dA * p.dconv;
                 const __half* srow = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
 #pragma unroll
@@ -954,9 +970,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             for (uint32_t g0 = 0, nt = 0; g0 < ntA && ok; g0 += nt) {
                 nt = g0 < tt.nsp ? min(TG, tt.nsp - g0) : min(TG, ntA - g0);
                 if (!consume_group(true, p.seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
-                if (ownA && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
+                const uint32_t ew = tid < EPI_T ? reinterpret_cast<const uint32_t*>(smem + OFF_EPI)[tid] : 0u;
+                const uint32_t rA = ew & 0xFFFFFu;
+                if ((ew & EPI_OWN) && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
                     __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
-                    if (convA) {
+                    if (ew & EPI_CONV) {
+                        const uint32_t dA = rA - p.di;
                         // conv-state roll + depthwise conv + SiLU (k_conv_update_silu_split arithmetic)
                         const uint4 cv = *reinterpret_cast<const uint4*>(smem + OFF_CONV + tid * 16);
                         const __half* cvh = reinterpret_cast<const __half*>(&cv);
@@ -979,8 +998,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         acc += __half2float(vh) * __half2float(wl);
                         vh = __float2half_rn(silu(__half2float(__float2half_rn(acc))));
                     }
-                    if (specA) mb_put(p.mb_in + (uint64_t)mA * p.proj + rA, mb_word(__half_as_ushort(vh), ep));
-                    else rowv[jA * 6 + (rowA < 8 ? 4 : 3)] = __half2float(vh);   // z / x of an own row
+                    if (ew & EPI_SPEC) mb_put(p.mb_in + (uint64_t)mA * p.proj + rA, mb_word(__half_as_ushort(vh), ep));
+                    else rowv[(ew >> 24) * 6 + (rowA < 8 ? 4 : 3)] = __half2float(vh);   // z / x of an own row
                 }
                 cons_sync();   // partial sums reused by the next group
             }
@@ -1244,7 +1263,8 @@ const char* decode_persist_plan(const PersistShape& sh, uint32_t* seg_in, uint32
     if ((uint64_t)sh.B * sh.dm * 2 > HBUF) return "hidden vectors exceed 10 KB";
     if (sh.di % 8 || sh.H * sh.P != sh.di) return "d_inner must be n_heads x d_head, a multiple of 8";
     const uint32_t nspec = (2 * sh.G * sh.N + sh.H + 15) / 16;
-    if (in_max_tiles(G, sh.di, nspec) * 16 * sh.B > CONS) return "too many in_proj rows per SM";
+    if (in_max_tiles(G, sh.di, nspec) * 16 * sh.B > EPI_T) return "too many in_proj rows per SM";
+    if (sh.proj >= (1u << 20)) return "in_proj wider than 2^20 rows";
     if (sh.dm / 4 > NOCT * CONS) return "d_model too wide for the residual pass (<= 2560)";
     if (sh.H % sh.G) return "n_heads not divisible by n_groups";
     if ((uint64_t)sh.B * 8 * in_max_units(G, sh.di, nspec) > SROWS) return "ssd state rows per SM exceed 40 KB";
