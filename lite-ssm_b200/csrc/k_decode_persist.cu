@@ -640,8 +640,9 @@ __device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
 }  // namespace
 
 // NB = sequences (1 or 2), a template parameter so that the one-sequence kernel keeps only
-// the accumulators it uses (11 warps allow 168 registers per thread).
-template <uint32_t NB>
+// the accumulators it uses (11 warps allow 168 registers per thread); TR = the phase trace
+// is recorded (p.trace set), so the untraced kernel carries no timer state.
+template <uint32_t NB, bool TR>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -799,7 +800,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                             uint32_t h0, h1;
                             in_tile_rows(tt, ti, G, p.di, h0, h1);
                             ok = put_in(mp, p.seg_in, h0, h1, c);
-                            if (p.trace && step == 0 && ti == 0 && c == 0)
+                            if (TR && step == 0 && ti == 0 && c == 0)
                                 p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
                         }
                     if (!ok) break;
@@ -814,7 +815,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         mbar_expect(bar, 16 * p.seg_lm * 128);
                         tma3(dst, ml, 0, (int32_t)(c * p.seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
                         advance();
-                        if (p.trace && step == 0 && ti == 0 && c == 0) p.trace[tbase + lmb + 5] = gtimer();
+                        if (TR && step == 0 && ti == 0 && c == 0) p.trace[tbase + lmb + 5] = gtimer();
                     }
             }
             // every issued copy must land before the CTA exits (bounded)
@@ -848,9 +849,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                 const uint32_t c0 = split ? u % nch : 0, c1 = split ? c0 + 1 : nch;
                 for (uint32_t c = c0; c < c1; ++c) {
                     if ((sn & 1) == half) {
-                        const uint64_t w0 = (p.trace && tid == 0) ? gtimer() : 0;
+                        const uint64_t w0 = (TR && tid == 0) ? gtimer() : 0;
                         if (!mbar_wait_ab(smem_u32(&full[slot]), phase, abort)) { bad = true; break; }
-                        if (p.trace && tid == 0) wait_ns += gtimer() - w0;
+                        if (TR && tid == 0) wait_ns += gtimer() - w0;
                         const uint8_t* stage = smem + OFF_RING + slot * STAGE;
                         if (int4)
                             consume_int4(stage, seg, c, reinterpret_cast<const uint4*>(xbuf), xsum, K / 8, K / 32,
@@ -927,7 +928,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     bool ok = true;
     for (uint32_t step = 0; step < p.n_steps && ok; ++step) {
-        const bool tr = p.trace && step == 0 && tid == 0;
+        const bool tr = TR && step == 0 && tid == 0;
         auto stamp = [&](uint32_t idx) {
             if (tr) p.trace[tbase + idx] = gtimer();
         };
@@ -1193,7 +1194,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 // the launch fails, so the grid barriers cannot wait on a CTA that never runs).
 cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s) {
     if (prm.B < 1 || prm.B > 2) return cudaErrorInvalidValue;
-    const void* fn = prm.B == 1 ? (const void*)k_decode_persist<1> : (const void*)k_decode_persist<2>;
+    const bool tr = prm.trace != nullptr;
+    const void* fn = prm.B == 1 ? (tr ? (const void*)k_decode_persist<1, true> : (const void*)k_decode_persist<1, false>)
+                                : (tr ? (const void*)k_decode_persist<2, true> : (const void*)k_decode_persist<2, false>);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
