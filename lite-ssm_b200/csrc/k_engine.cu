@@ -71,7 +71,7 @@ __global__ void k_conv_silu_split(const __half* __restrict__ xbc, uint64_t in_st
 // Vectorised form (d_conv == 4, 8 channels per thread, 16-byte loads and stores): the
 // same arithmetic per channel. Needs in_stride, d_inner and GN multiples of 8 and 16-byte
 // aligned rows, so an octet never straddles the x / B / C boundaries.
-constexpr uint32_t CT8 = 16;   // tokens per thread
+constexpr uint32_t CT8 = 8;    // tokens per thread
 constexpr uint32_t CU8 = 8;    // rows loaded together (independent loads in flight per thread)
 __global__ void __launch_bounds__(128) k_conv4_silu_split8(const __half* __restrict__ xbc, uint64_t in_stride,
                                                            const __half* __restrict__ w,

@@ -23,6 +23,7 @@
 
 #include "device_util.cuh"
 #include "lssm_internal.h"
+#include "mma_int4.cuh"
 #include "tc_common.cuh"
 
 namespace lssm {
@@ -354,30 +355,59 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
 
 // ---------------------------------------------------------------------------
 //  INT4_B32 -> fp16 dequantisation (shaders/linear.metal:38-61, rounded to fp16 like
-//  the reference GEMM tile, linear.metal:538). One thread per 32-weight block.
+//  the reference GEMM tile, linear.metal:538: half(float(q) * scale)). One thread per
+//  32-weight block: one 16-byte load of its packed nibbles, four 16-byte stores. The
+//  nibbles become exact fp16 q values (dequant_word), and one HMUL2 by the block's scale
+//  gives half(q * s) rounded once, the same value as the fp32 product rounded to fp16
+//  (q * s is exact in fp32); a byte permute restores the k order.
 // ---------------------------------------------------------------------------
-__global__ void k_int4_dequant(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
-                               __half* __restrict__ out, uint32_t N, uint32_t K) {
+__global__ void __launch_bounds__(256) k_int4_dequant(const uint8_t* __restrict__ packed,
+                                                      const __half* __restrict__ scales, __half* __restrict__ out,
+                                                      uint32_t N, uint32_t K) {
+    const uint32_t nb = K / 32;
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)N * nb) return;
+    const uint64_t row = i / nb, b = i % nb;
+    const uint4 pk = __ldcs(reinterpret_cast<const uint4*>(packed + row * (K / 2) + b * 16));
+    const __half2 s2 = __half2half2(scales[i]);
+    const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+    uint4 o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t q[4];   // exact fp16 q pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7) of word j
+        dequant_word(w4[j], q);
+        uint32_t v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
+            v[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        o[j].x = __byte_perm(v[0], v[1], 0x5410);   // k0 k1
+        o[j].y = __byte_perm(v[2], v[3], 0x5410);   // k2 k3
+        o[j].z = __byte_perm(v[0], v[1], 0x7632);   // k4 k5
+        o[j].w = __byte_perm(v[2], v[3], 0x7632);   // k6 k7
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + row * K + b * 32);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = o[j];
+}
+
+// Any alignment (a packed matrix at an odd offset of a .ssm payload): byte loads.
+__global__ void k_int4_dequant_bytes(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
+                                     __half* __restrict__ out, uint32_t N, uint32_t K) {
     const uint32_t nb = K / 32;
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)N * nb) return;
     const uint64_t row = i / nb, b = i % nb;
     const uint8_t* src = packed + row * (K / 2) + b * 16;
-    const float s = __half2float(scales[row * nb + b]);
-    __half h[32];
+    const float s = __half2float(scales[i]);
+    __half* dst = out + row * K + b * 32;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const uint8_t byte = src[j];
         const int lo = byte & 0xF, hi = byte >> 4;
-        h[2 * j] = __float2half_rn((float)(lo < 8 ? lo : lo - 16) * s);
-        h[2 * j + 1] = __float2half_rn((float)(hi < 8 ? hi : hi - 16) * s);
-    }
-    __half* dst = out + row * K + b * 32;
-    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = reinterpret_cast<uint4*>(h)[j];
-    } else {
-        for (int j = 0; j < 32; ++j) dst[j] = h[j];
+        dst[2 * j] = __float2half_rn((float)(lo < 8 ? lo : lo - 16) * s);
+        dst[2 * j + 1] = __float2half_rn((float)(hi < 8 ? hi : hi - 16) * s);
     }
 }
 
@@ -385,6 +415,13 @@ cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void
                                     cudaStream_t s) {
     const uint64_t n = (uint64_t)N * (K / 32);
     if (!n) return cudaSuccess;
+    // 16-byte loads and stores: K % 32 == 0 keeps every block aligned once the bases are
+    if ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(out)) & 15) {
+        k_int4_dequant_bytes<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                                      static_cast<const __half*>(scales),
+                                                                      static_cast<__half*>(out), N, K);
+        return cudaGetLastError();
+    }
     k_int4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(packed),
                                                               static_cast<const __half*>(scales),
                                                               static_cast<__half*>(out), N, K);

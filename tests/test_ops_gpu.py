@@ -205,6 +205,40 @@ def test_linear_int4_gemm(ctx, ops, M, N, K):
     close(get16(by, M * N), po.to_f32(ref), rtol=1e-2, atol=2e-3)
 
 
+# off 2: the packed nibbles at an unaligned offset of a payload (byte-load fallback)
+@pytest.mark.parametrize("off", [0, 2])
+def test_int4_dequantised_weights_bit_exact(ctx, ops, off):
+    """M > 512 takes the dequantise-then-GEMM path. With unit-vector activation rows the GEMM
+    returns single weights (one exact product, fp32 sum, fp16 result), so each output must
+    equal half(float(q) * float(scale)) bit for bit (linear.metal:538 rounding), including
+    scales whose products round near the fp16 maximum, go subnormal and carry both signs
+    (finite products only: an infinite weight times a zero activation would be NaN; zeros
+    compare without their sign)."""
+    M, N, K = 600, 304, 2560
+    packed, scales = _int4_weights(N, K)
+    sc = scales.view(np.float16).copy()
+    sc.ravel()[:7] = np.float16([4000, -4000, 6e-8, -3e-6, 0.0, 1.5e-5, -7e3])
+    scales = sc.view(np.uint16)
+    ks = RNG.choice(K, size=M, replace=True)
+    x = np.zeros((M, K), np.float16)
+    x[np.arange(M), ks] = 1.0
+    nib = np.zeros((N, K), np.int32)
+    nib[:, 0::2] = packed & 0xF
+    nib[:, 1::2] = packed >> 4
+    q = np.where(nib < 8, nib, nib - 16).astype(np.float32)
+    w16 = (q * np.repeat(scales.view(np.float16).astype(np.float32), 32, axis=1)).astype(np.float16)
+    blob = np.concatenate([np.zeros(off, np.uint8), packed.ravel()])
+    bp_, bs, bx, by = hb(ctx, blob), hb(ctx, scales), hb(ctx, x), lssm.DeviceBuffer(ctx, M * N * 2)
+    ops.linear_int4_gemm((bx, 0), (bp_, off), (bs, 0), (by, 0), lssm.LinearDims(M, N, K))
+    got = by.download(np.uint16, M * N).reshape(M, N)
+    # the GEMM's fp32 sum starts at +0, so a -0 weight (q = 0 with a negative scale) comes out as +0
+    want = np.where(w16[:, ks].T == 0, np.float16(0), w16[:, ks].T).astype(np.float16).view(np.uint16)
+    bad = np.argwhere(got != want)
+    detail = [(int(m), int(n), int(ks[m]), hex(int(got[m, n])), hex(int(want[m, n])),
+               float(scales.view(np.float16)[n, ks[m] // 32])) for m, n in bad[:8]]
+    assert not len(bad), f"{len(bad)} dequantised weights differ (m, n, k, got, want, scale): {detail}"
+
+
 def test_int4_gemm_scratch_growth_keeps_replayed_graph_valid():
     """The INT4 GEMM's scratch belongs to the context. A captured batch keeps using its block
     after a later, larger call grows the scratch outside the batch (the old block is kept
