@@ -356,40 +356,32 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
 // ---------------------------------------------------------------------------
 //  INT4_B32 -> fp16 dequantisation (shaders/linear.metal:38-61, rounded to fp16 like
 //  the reference GEMM tile, linear.metal:538: half(float(q) * scale)). One thread per
-//  32-weight block: one 16-byte load of its packed nibbles, four 16-byte stores. The
-//  nibbles become exact fp16 q values (dequant_word), and one HMUL2 by the block's scale
-//  gives half(q * s) rounded once, the same value as the fp32 product rounded to fp16
-//  (q * s is exact in fp32); a byte permute restores the k order.
+//  packed 32-bit word (8 weights): a warp reads 128 contiguous bytes and writes 512
+//  contiguous bytes (one 16-byte store per thread). The nibbles become exact fp16 q values
+//  (dequant_word), and one HMUL2 by the block's scale gives half(q * s) rounded once, the
+//  same value as the fp32 product rounded to fp16 (q * s is exact in fp32); a byte permute
+//  restores the k order.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_int4_dequant(const uint8_t* __restrict__ packed,
-                                                      const __half* __restrict__ scales, __half* __restrict__ out,
-                                                      uint32_t N, uint32_t K) {
-    const uint32_t nb = K / 32;
+__global__ void __launch_bounds__(256) k_int4_dequant(const uint32_t* __restrict__ packed,
+                                                      const __half* __restrict__ scales, uint4* __restrict__ out,
+                                                      uint64_t n_words, uint32_t words_per_row) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (uint64_t)N * nb) return;
-    const uint64_t row = i / nb, b = i % nb;
-    const uint4 pk = __ldcs(reinterpret_cast<const uint4*>(packed + row * (K / 2) + b * 16));
-    const __half2 s2 = __half2half2(scales[i]);
-    const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-    uint4 o[4];
+    if (i >= n_words) return;
+    const uint64_t row = i / words_per_row, wr = i % words_per_row;
+    const uint32_t w = __ldcs(packed + i);   // rows are contiguous: word i of the matrix
+    const __half2 s2 = __half2half2(scales[row * (words_per_row / 4) + wr / 4]);
+    uint32_t q[4];   // exact fp16 q pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7)
+    dequant_word(w, q);
+    uint32_t v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        uint32_t q[4];   // exact fp16 q pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7) of word j
-        dequant_word(w4[j], q);
-        uint32_t v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
-            v[e] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        o[j].x = __byte_perm(v[0], v[1], 0x5410);   // k0 k1
-        o[j].y = __byte_perm(v[2], v[3], 0x5410);   // k2 k3
-        o[j].z = __byte_perm(v[0], v[1], 0x7632);   // k4 k5
-        o[j].w = __byte_perm(v[2], v[3], 0x7632);   // k6 k7
+    for (int e = 0; e < 4; ++e) {
+        const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&q[e]), s2);
+        v[e] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    uint4* dst = reinterpret_cast<uint4*>(out + row * K + b * 32);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = o[j];
+    out[i] = make_uint4(__byte_perm(v[0], v[1], 0x5410),    // k0 k1
+                        __byte_perm(v[2], v[3], 0x5410),    // k2 k3
+                        __byte_perm(v[0], v[1], 0x7632),    // k4 k5
+                        __byte_perm(v[2], v[3], 0x7632));   // k6 k7
 }
 
 // Any alignment (a packed matrix at an odd offset of a .ssm payload): byte loads.
@@ -415,16 +407,17 @@ cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void
                                     cudaStream_t s) {
     const uint64_t n = (uint64_t)N * (K / 32);
     if (!n) return cudaSuccess;
-    // 16-byte loads and stores: K % 32 == 0 keeps every block aligned once the bases are
-    if ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(out)) & 15) {
+    // 4-byte loads and 16-byte stores: K % 32 == 0 keeps every word aligned once the bases are
+    if ((reinterpret_cast<uintptr_t>(packed) & 3) | (reinterpret_cast<uintptr_t>(out) & 15)) {
         k_int4_dequant_bytes<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(packed),
                                                                       static_cast<const __half*>(scales),
                                                                       static_cast<__half*>(out), N, K);
         return cudaGetLastError();
     }
-    k_int4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t*>(packed),
-                                                              static_cast<const __half*>(scales),
-                                                              static_cast<__half*>(out), N, K);
+    const uint64_t n_words = (uint64_t)N * (K / 8);
+    k_int4_dequant<<<(unsigned)((n_words + 255) / 256), 256, 0, s>>>(static_cast<const uint32_t*>(packed),
+                                                                    static_cast<const __half*>(scales),
+                                                                    static_cast<uint4*>(out), n_words, K / 8);
     return cudaGetLastError();
 }
 
