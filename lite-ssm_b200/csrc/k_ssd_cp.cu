@@ -111,11 +111,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
                  "r"(src), "r"(c0), "r"(c1), "r"(c2)
                  : "memory");
 }
-__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
-                 "r"(src), "r"(bytes)
-                 : "memory");
-}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -390,9 +385,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_ld32(tmem + lane_base + T_SC + 64 * g + hc * 32, v);
             tc::tmem_ld_wait();
             if (c + 1 < nc) {
-                // staged in the group's X / X~ buffers (free: Y and S_c are done) in the ring's
-                // layout, then stored by one bulk copy
-                float4* dst = reinterpret_cast<float4*>(gX) + hc * 8 * TN + t;
+                // stored straight from registers into ring slot c & 1 ([16 p-quads][128 n][4]:
+                // a warp's 32 lanes write 512 contiguous bytes per store); published below
+                float4* dst = reinterpret_cast<float4*>(
+                                  a.ring + (((uint64_t)(c & 1) * a.batch + b) * a.H + h) * TN * TP) +
+                              hc * 8 * TN + t;
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     dst[j * TN] = make_float4(dch * sin[4 * j] + __uint_as_float(v[4 * j]),
@@ -426,12 +423,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tc::umma_f16(tmem + T_CB + 64 * g, tc::sw128_desc(sCa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
                              tc::sw128_desc(sSa + k * 2048, PANEL, 1024), ID_Y, k > 0);
             tc::umma_commit(bar_cs);
-            // publish S_out of chunk c while CS runs: bulk store, wait for its writes, then the counter
+            // publish S_out of chunk c while CS runs: the group's stores (ordered before this
+            // thread by the group barrier) are released by one gpu-scope fence, then the counter
             if (c + 1 < nc) {
-                bulk_store(a.ring + (((uint64_t)(c & 1) * a.batch + b) * a.H + h) * TN * TP, smem_u32(gX), TN * TP * 4);
-                bulk_commit();
-                bulk_wait_all();
-                asm volatile("fence.proxy.async.global;" ::: "memory");
                 asm volatile("fence.acq_rel.gpu;" ::: "memory");
                 asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.count + (uint64_t)b * a.H + h), "r"(c + 1)
                              : "memory");
