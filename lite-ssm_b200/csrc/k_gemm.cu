@@ -13,7 +13,8 @@
 //                 per instruction), tcgen05.commit frees ring stages / publishes a
 //                 finished accumulator.
 //   warps 2..5    epilogue: tcgen05.ld (32 lanes x 32 columns) -> fp16 -> global.
-//   The fp32 accumulator is double buffered in TMEM (2 x BN columns), so the
+//   The fp32 accumulator is double buffered in TMEM (two BN-column buffers, each from a
+//   32-column boundary; BN % 32 == 16 ends in a 16-column chunk), so the
 //   epilogue of tile i overlaps the main loop of tile i+1.
 // All waits are bounded (tc_common.cuh); a timeout raises the kernel's error word.
 #include <cuda.h>
@@ -71,7 +72,8 @@ struct GemmCfg {
     static constexpr int B_BYTES = BN * GEMM_BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 6 ? 6 : (200 * 1024) / STAGE_BYTES;
-    static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+    static constexpr int ACC = (BN + 31) / 32 * 32;   // TMEM columns per accumulator buffer (32-aligned starts)
+    static constexpr int TMEM_COLS = (2 * ACC <= 256) ? 256 : 512;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
                 if (!tc::mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag)) break;
                 tc::tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * Cfg::ACC;
                 bool ok = true;
                 for (uint32_t kb = 0; kb < nk; ++kb) {
                     if (!tc::mbar_wait(smem_u32(&full[stage]), phase, abort_flag)) { ok = false; break; }
@@ -179,44 +181,47 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!tc::mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag)) break;
             tc::tc_fence_after();
             const uint32_t row = mb * GEMM_BM + q * 32 + lane;
+            // 32-column chunks; with BN % 32 == 16 the last chunk is 16 columns wide
+            constexpr uint32_t NCH = (BN + 31) / 32;
 #pragma unroll 1
-            for (uint32_t ch = 0; ch < (uint32_t)BN / 32; ++ch) {
+            for (uint32_t ch = 0; ch < NCH; ++ch) {
+                const uint32_t cw = (BN % 32 != 0 && ch == NCH - 1) ? 16u : 32u;
                 uint32_t v[32];
-                tc::tmem_ld32(tmem_base + acc * BN + ch * 32 + ((q * 32) << 16), v);
+                if (cw == 32) tc::tmem_ld32(tmem_base + acc * Cfg::ACC + ch * 32 + ((q * 32) << 16), v);
+                else tc::tmem_ld16(tmem_base + acc * Cfg::ACC + ch * 32 + ((q * 32) << 16), *reinterpret_cast<uint32_t(*)[16]>(v));
                 tc::tmem_ld_wait();
                 const uint32_t col0 = nb * BN + ch * 32;
+                const bool full = vec && col0 + cw <= N;
                 if (row < M && col0 < N && epilogue == 3) {
                     // fp32 output (partial sums that a collective adds before rounding)
                     float* yf = reinterpret_cast<float*>(Y) + (uint64_t)row * ldy + col0;
-                    if (vec && col0 + 32 <= N && (ldy % 4 == 0)) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(yf)[j] = reinterpret_cast<uint4*>(v)[j];
+                    if (full && (ldy % 4 == 0)) {
+                        for (uint32_t j = 0; j < cw / 4; ++j) reinterpret_cast<uint4*>(yf)[j] = reinterpret_cast<uint4*>(v)[j];
                     } else {
-                        for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) yf[j] = __uint_as_float(v[j]);
+                        for (uint32_t j = 0; j < cw && col0 + j < N; ++j) yf[j] = __uint_as_float(v[j]);
                     }
                 } else if (row < M && col0 < N) {
                     __half h[32];
                     __half* yr = Y + (uint64_t)row * ldy + col0;
                     if (epilogue == 2) {   // residual: y = half(y + half(acc)) (mamba2_block.cpp:274-276)
-                        if (vec && col0 + 32 <= N) {
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(h)[j] = reinterpret_cast<const uint4*>(yr)[j];
+                        if (full) {
+                            for (uint32_t j = 0; j < cw / 8; ++j) reinterpret_cast<uint4*>(h)[j] = reinterpret_cast<const uint4*>(yr)[j];
                         } else {
-                            for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) h[j] = yr[j];
+                            for (uint32_t j = 0; j < cw && col0 + j < N; ++j) h[j] = yr[j];
                         }
                     }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
+                        if ((uint32_t)j >= cw) break;
                         float f = __uint_as_float(v[j]);
                         if (epilogue == 1) f = silu(f);
                         if (epilogue == 2) f = __half2float(h[j]) + __half2float(__float2half_rn(f));
                         h[j] = __float2half_rn(f);
                     }
-                    if (vec && col0 + 32 <= N) {
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(yr)[j] = reinterpret_cast<uint4*>(h)[j];
+                    if (full) {
+                        for (uint32_t j = 0; j < cw / 8; ++j) reinterpret_cast<uint4*>(yr)[j] = reinterpret_cast<uint4*>(h)[j];
                     } else {
-                        for (uint32_t j = 0; j < 32 && col0 + j < N; ++j) yr[j] = h[j];
+                        for (uint32_t j = 0; j < cw && col0 + j < N; ++j) yr[j] = h[j];
                     }
                 }
             }
@@ -338,7 +343,7 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
     const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
     double best = -1.0;
     int best_bn = 256;
-    const int cands[4] = {256, 192, 160, 128};
+    const int cands[6] = {256, 240, 192, 160, 144, 128};
     for (int c : cands) {
         const uint32_t tiles = mt * ((N + c - 1) / c);
         const uint32_t waves = (tiles + sms - 1) / sms;
@@ -349,7 +354,9 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
     }
     if (best_bn == 256) return run_gemm_tc<256>(x, w, y, M, N, K, epilogue, sms, s);
     if (best_bn == 192) return run_gemm_tc<192>(x, w, y, M, N, K, epilogue, sms, s);
+    if (best_bn == 240) return run_gemm_tc<240>(x, w, y, M, N, K, epilogue, sms, s);
     if (best_bn == 160) return run_gemm_tc<160>(x, w, y, M, N, K, epilogue, sms, s);
+    if (best_bn == 144) return run_gemm_tc<144>(x, w, y, M, N, K, epilogue, sms, s);
     return run_gemm_tc<128>(x, w, y, M, N, K, epilogue, sms, s);
 }
 

@@ -114,8 +114,10 @@ def test_rmsnorm_linear_gemv(ctx, ops):
     close(get16(by, N), po.to_f32(ref))
 
 
+# (2048, 2560, 5120) takes 144-wide N tiles (last tile ragged), (2048, 10576, 2560) 240-wide ones:
+# accumulators ending in a 16-column chunk
 @pytest.mark.parametrize("M,N,K", [(200, 300, 256), (130, 257, 72), (512, 1024, 2560), (33, 40, 36), (1, 16, 64),
-                                   (2048, 2560, 5120)])
+                                   (2048, 2560, 5120), (2048, 10576, 2560)])
 def test_linear_f16_gemm(ctx, ops, M, N, K):
     x = h(RNG.standard_normal((M, K)))
     w = h(RNG.standard_normal((N, K)) / np.sqrt(K))
