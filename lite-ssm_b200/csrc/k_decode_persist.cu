@@ -641,8 +641,9 @@ __device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
 
 // NB = sequences (1 or 2), a template parameter so that the one-sequence kernel keeps only
 // the accumulators it uses (11 warps allow 168 registers per thread); TR = the phase trace
-// is recorded (p.trace set), so the untraced kernel carries no timer state.
-template <uint32_t NB, bool TR>
+// is recorded (p.trace set), so the untraced kernel carries no timer state; SEG = 5 when every
+// streamed chunk has 5 segments (the 2.7B shapes), else 0 (read from p).
+template <uint32_t NB, bool TR, uint32_t SEG>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -670,7 +671,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
     const uint32_t nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
-    const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
+    // SEG != 0: every streamed chunk has SEG segments (known at compile time: the segment
+    // arithmetic of the consume loops folds into immediates)
+    const uint32_t seg_in = SEG ? SEG : p.seg_in, seg_out = SEG ? SEG : p.seg_out, seg_lm = SEG ? SEG : p.seg_lm;
+    const uint32_t nchA = p.dm / (seg_in * 256), nchC = p.di / (seg_out * 256), nchL = p.dm / (seg_lm * 64);
     const uint32_t uC = nC * nchC;                                  // out_proj (tile, chunk) units
     const uint32_t nspec = (2 * p.G * p.N + p.H + 15) / 16;        // B / C / dt tiles
     const InTiles tt = in_tiles(cta, G, p.di, nspec);
@@ -684,12 +688,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
-    if (p.dconv > 4 || p.dconv < 1 || NB > 2 || NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
+    if ((SEG && (p.seg_in != SEG || p.seg_out != SEG || p.seg_lm != SEG)) || p.dconv > 4 || p.dconv < 1 || NB > 2 ||
+        NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
         NB * 8 * in_max_units(G, p.di, nspec) > SROWS || p.di % 8 || p.H * p.P != p.di ||
         p.n_layer > LT_MAX || (uint64_t)NB * max(p.dm, p.di) * 2 > XBUF || (uint64_t)NB * p.dm * 2 > HBUF ||
-        p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
-        p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
-        nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
+        p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || seg_in > SEG_MAX || seg_out > SEG_MAX ||
+        seg_lm > SEG_MAX || !(seg_in & 1) || !(seg_out & 1) || !(seg_lm & 1) || nchA * seg_in * 256 != p.dm ||
+        nchC * seg_out * 256 != p.di || nchL * seg_lm * 64 != p.dm || nchC > NCH_MAX ||
         p.H % p.G || in_max_tiles(G, p.di, nspec) * 16 * NB > EPI_T || p.dm / 4 > NOCT * CONS ||
         p.proj >= (1u << 20)) {
         if (tid == 0) atomicExch(p.err, 1);
@@ -799,12 +804,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         for (uint32_t c = 0; c < nchA && ok; ++c) {
                             uint32_t h0, h1;
                             in_tile_rows(tt, ti, G, p.di, h0, h1);
-                            ok = put_in(mp, p.seg_in, h0, h1, c);
+                            ok = put_in(mp, seg_in, h0, h1, c);
                             if (TR && step == 0 && ti == 0 && c == 0)
                                 p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
                         }
                     if (!ok) break;
-                    for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, p.seg_out, cta + i * G, nchC);
+                    for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, seg_out, cta + i * G, nchC);
                 }
                 const CUtensorMap* ml = maps + 4 * p.n_layer;
                 for (uint32_t ti = 0; ti < ntL && ok; ++ti)
@@ -812,8 +817,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         const uint32_t s = take();
                         if (s == ~0u) { ok = false; break; }
                         const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
-                        mbar_expect(bar, 16 * p.seg_lm * 128);
-                        tma3(dst, ml, 0, (int32_t)(c * p.seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
+                        mbar_expect(bar, 16 * seg_lm * 128);
+                        tma3(dst, ml, 0, (int32_t)(c * seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
                         advance();
                         if (TR && step == 0 && ti == 0 && c == 0) p.trace[tbase + lmb + 5] = gtimer();
                     }
@@ -970,7 +975,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             // special tiles form their own group(s), so their rows are published before the units run
             for (uint32_t g0 = 0, nt = 0; g0 < ntA && ok; g0 += nt) {
                 nt = g0 < tt.nsp ? min(TG, tt.nsp - g0) : min(TG, ntA - g0);
-                if (!consume_group(true, p.seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
+                if (!consume_group(true, seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
                 const uint32_t ew = tid < EPI_T ? reinterpret_cast<const uint32_t*>(smem + OFF_EPI)[tid] : 0u;
                 const uint32_t rA = ew & 0xFFFFFu;
                 if ((ew & EPI_OWN) && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
@@ -1113,7 +1118,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
             stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, NB, p.di, true, xbuf, xsum, red);
             stamp(lb + 6);
-            if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
+            if (!gemv_phase(seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
 
             if (!grid_sync(p, gen, abort)) { ok = false; break; }
@@ -1127,7 +1132,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         uint32_t bi = 0xFFFFFFFFu;
         for (uint32_t g0 = 0; g0 < ntL && ok; g0 += TG) {
             const uint32_t nt = min(TG, ntL - g0);
-            if (!consume_group(false, p.seg_lm, nchL, p.dm, false, g0, nt)) { ok = false; break; }
+            if (!consume_group(false, seg_lm, nchL, p.dm, false, g0, nt)) { ok = false; break; }
             if (tid < nt * 16 * NB) {
                 const uint32_t ti = tid / (16 * NB), row = (tid / NB) % 16, m = tid % NB;
                 const uint32_t r = (cta + (g0 + ti) * G) * 16 + row;
@@ -1195,8 +1200,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s) {
     if (prm.B < 1 || prm.B > 2) return cudaErrorInvalidValue;
     const bool tr = prm.trace != nullptr;
-    const void* fn = prm.B == 1 ? (tr ? (const void*)k_decode_persist<1, true> : (const void*)k_decode_persist<1, false>)
-                                : (tr ? (const void*)k_decode_persist<2, true> : (const void*)k_decode_persist<2, false>);
+    const bool s5 = prm.seg_in == 5 && prm.seg_out == 5 && prm.seg_lm == 5;
+    const void* fn;
+    if (prm.B == 1)
+        fn = s5 ? (tr ? (const void*)k_decode_persist<1, true, 5> : (const void*)k_decode_persist<1, false, 5>)
+                : (tr ? (const void*)k_decode_persist<1, true, 0> : (const void*)k_decode_persist<1, false, 0>);
+    else
+        fn = s5 ? (tr ? (const void*)k_decode_persist<2, true, 5> : (const void*)k_decode_persist<2, false, 5>)
+                : (tr ? (const void*)k_decode_persist<2, true, 0> : (const void*)k_decode_persist<2, false, 0>);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
