@@ -641,14 +641,10 @@ __device__ __forceinline__ void warp_argmax(float& v, uint32_t& i, uint32_t B) {
 
 // NB = sequences (1 or 2), a template parameter so that the one-sequence kernel keeps only
 // the accumulators it uses (11 warps allow 168 registers per thread); TR = the phase trace
-// is recorded (p.trace set), so the untraced kernel carries no timer state; SEG = 5 when every
-// streamed chunk has 5 segments, else 0 (read from p); DM = 2560 for the 2.7B shape (d_model
-// 2560, d_inner 5120), else 0.
-template <uint32_t NB, bool TR, uint32_t SEG, uint32_t DM>
+// is recorded (p.trace set), so the untraced kernel carries no timer state.
+template <uint32_t NB, bool TR>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    // DM != 0: d_model == DM and d_inner == 2 DM (compile-time: sizes and loop bounds fold)
-    const uint32_t dm = DM ? DM : p.dm, di = DM ? 2 * DM : p.di;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + RING;
     uint64_t* sfull = empty + RING;       // ssd state rows landed
@@ -673,14 +669,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
-    const uint32_t nC = (dm + 15) / 16, nL = (p.V + 15) / 16;
-    // SEG != 0: every streamed chunk has SEG segments (known at compile time: the segment
-    // arithmetic of the consume loops folds into immediates)
-    const uint32_t seg_in = SEG ? SEG : p.seg_in, seg_out = SEG ? SEG : p.seg_out, seg_lm = SEG ? SEG : p.seg_lm;
-    const uint32_t nchA = dm / (seg_in * 256), nchC = di / (seg_out * 256), nchL = dm / (seg_lm * 64);
+    const uint32_t nC = (p.dm + 15) / 16, nL = (p.V + 15) / 16;
+    const uint32_t nchA = p.dm / (p.seg_in * 256), nchC = p.di / (p.seg_out * 256), nchL = p.dm / (p.seg_lm * 64);
     const uint32_t uC = nC * nchC;                                  // out_proj (tile, chunk) units
     const uint32_t nspec = (2 * p.G * p.N + p.H + 15) / 16;        // B / C / dt tiles
-    const InTiles tt = in_tiles(cta, G, di, nspec);
+    const InTiles tt = in_tiles(cta, G, p.di, nspec);
     const uint32_t ntA = tt.nsp + tt.nu;                            // this CTA's in_proj tiles
     const uint32_t nuC = cta < uC ? (uC - 1 - cta) / G + 1 : 0;    // this CTA's out_proj units
     const uint32_t ntL = cta < nL ? (nL - 1 - cta) / G + 1 : 0;    // lm_head tiles
@@ -691,15 +684,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 
     // Shapes the host checks before choosing this kernel, re-checked (identically in
     // every CTA) so a bad launch reports an error instead of overrunning shared memory.
-    if ((SEG && (p.seg_in != SEG || p.seg_out != SEG || p.seg_lm != SEG)) || (DM && (p.dm != DM || p.di != 2 * DM)) ||
-        p.dconv > 4 || p.dconv < 1 || NB > 2 ||
-        NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
-        NB * 8 * in_max_units(G, di, nspec) > SROWS || di % 8 || p.H * p.P != di ||
-        p.n_layer > LT_MAX || (uint64_t)NB * max(dm, di) * 2 > XBUF || (uint64_t)NB * dm * 2 > HBUF ||
-        dm / 8 > NOCT * CONS || di / 8 > NOCT * CONS || seg_in > SEG_MAX || seg_out > SEG_MAX ||
-        seg_lm > SEG_MAX || !(seg_in & 1) || !(seg_out & 1) || !(seg_lm & 1) || nchA * seg_in * 256 != dm ||
-        nchC * seg_out * 256 != di || nchL * seg_lm * 64 != dm || nchC > NCH_MAX ||
-        p.H % p.G || in_max_tiles(G, di, nspec) * 16 * NB > EPI_T || dm / 4 > NOCT * CONS ||
+    if (p.dconv > 4 || p.dconv < 1 || NB > 2 || NB < 1 || p.N != 128 || p.P < 32 || p.P > 256 || p.H > 65535 ||
+        NB * 8 * in_max_units(G, p.di, nspec) > SROWS || p.di % 8 || p.H * p.P != p.di ||
+        p.n_layer > LT_MAX || (uint64_t)NB * max(p.dm, p.di) * 2 > XBUF || (uint64_t)NB * p.dm * 2 > HBUF ||
+        p.dm / 8 > NOCT * CONS || p.di / 8 > NOCT * CONS || p.seg_in > SEG_MAX || p.seg_out > SEG_MAX ||
+        p.seg_lm > SEG_MAX || !(p.seg_in & 1) || !(p.seg_out & 1) || !(p.seg_lm & 1) || nchA * p.seg_in * 256 != p.dm ||
+        nchC * p.seg_out * 256 != p.di || nchL * p.seg_lm * 64 != p.dm || nchC > NCH_MAX ||
+        p.H % p.G || in_max_tiles(G, p.di, nspec) * 16 * NB > EPI_T || p.dm / 4 > NOCT * CONS ||
         p.proj >= (1u << 20)) {
         if (tid == 0) atomicExch(p.err, 1);
         return;
@@ -797,7 +788,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         mbar_expect(smem_u32(sfull), sbytes);
                         for (uint32_t m = 0; m < NB; ++m)
                             bulk_g2s(smem_u32(smem + OFF_S + m * urows * p.N * 4),
-                                     LT[l].ssd_state + ((uint64_t)m * di + 8 * tt.ub) * p.N, urows * p.N * 4,
+                                     LT[l].ssd_state + ((uint64_t)m * p.di + 8 * tt.ub) * p.N, urows * p.N * 4,
                                      smem_u32(sfull));
                     } else {
                         mbar_arrive1(smem_u32(sfull));
@@ -807,13 +798,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     for (uint32_t ti = 0; ti < ntA && ok; ++ti)
                         for (uint32_t c = 0; c < nchA && ok; ++c) {
                             uint32_t h0, h1;
-                            in_tile_rows(tt, ti, G, di, h0, h1);
-                            ok = put_in(mp, seg_in, h0, h1, c);
+                            in_tile_rows(tt, ti, G, p.di, h0, h1);
+                            ok = put_in(mp, p.seg_in, h0, h1, c);
                             if (TR && step == 0 && ti == 0 && c == 0)
                                 p.trace[tbase + l * TRACE_PER_LAYER + 8] = gtimer();
                         }
                     if (!ok) break;
-                    for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, seg_out, cta + i * G, nchC);
+                    for (uint32_t i = 0; i < nuC && ok; ++i) ok = put_int4(mp + 2, p.seg_out, cta + i * G, nchC);
                 }
                 const CUtensorMap* ml = maps + 4 * p.n_layer;
                 for (uint32_t ti = 0; ti < ntL && ok; ++ti)
@@ -821,8 +812,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         const uint32_t s = take();
                         if (s == ~0u) { ok = false; break; }
                         const uint32_t dst = smem_u32(smem + OFF_RING + s * STAGE), bar = smem_u32(&full[s]);
-                        mbar_expect(bar, 16 * seg_lm * 128);
-                        tma3(dst, ml, 0, (int32_t)(c * seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
+                        mbar_expect(bar, 16 * p.seg_lm * 128);
+                        tma3(dst, ml, 0, (int32_t)(c * p.seg_lm), (int32_t)((cta + ti * G) * 16), bar, pol);
                         advance();
                         if (TR && step == 0 && ti == 0 && c == 0) p.trace[tbase + lmb + 5] = gtimer();
                     }
@@ -925,10 +916,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         uint32_t w = 0;
         if (tiA < ntA) {
             uint32_t hA0, hA1;
-            in_tile_rows(tt, tiA, G, di, hA0, hA1);
+            in_tile_rows(tt, tiA, G, p.di, hA0, hA1);
             const uint32_t rA = rowA < 8 ? hA0 + rowA : hA1 + rowA - 8;   // in_proj output row
             w = rA | EPI_OWN;
-            if (rA >= di && rA < di + p.xd) w |= EPI_CONV;
+            if (rA >= p.di && rA < p.di + p.xd) w |= EPI_CONV;
             if (tiA < tt.nsp) w |= EPI_SPEC;                               // B / C / dt rows: published
             else w |= (mA * urows + (tiA - tt.nsp) * 8 + (rowA & 7)) << 24;   // unit rows: local state row
         }
@@ -955,7 +946,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             const uint32_t ew0 = tid < EPI_T ? reinterpret_cast<const uint32_t*>(smem + OFF_EPI)[tid] : 0u;
             const bool convA = ew0 & EPI_CONV;
             if (convA) {
-                const uint32_t dA = (ew0 & 0xFFFFFu) - di;
+                const uint32_t dA = (ew0 & 0xFFFFFu) - p.di;
                 const __half* wrow = L.conv_w + (uint64_t)dA * p.dconv;
                 const __half* srow = L.conv_state + ((uint64_t)mA * p.xd + dA) * p.dconv;
 #pragma unroll
@@ -965,7 +956,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             }
             // ---- A: residual + RMSNorm, in_proj tiles (all K chunks of a tile), epilogue:
             // z / dt and, for xBC rows, conv-state roll + conv + SiLU -> exchange words
-            stage_norm_h<NB>(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, dm, true, xbuf, xsum,
+            stage_norm_h<NB>(p.opart, nchC, l == 0 ? tok : nullptr, p.embed, hid, L.norm_w, p.dm, true, xbuf, xsum,
                          red);
             // park the conv inputs in this thread's shared-memory slot: no registers held across in_proj
             if (convA) {
@@ -979,13 +970,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             // special tiles form their own group(s), so their rows are published before the units run
             for (uint32_t g0 = 0, nt = 0; g0 < ntA && ok; g0 += nt) {
                 nt = g0 < tt.nsp ? min(TG, tt.nsp - g0) : min(TG, ntA - g0);
-                if (!consume_group(true, seg_in, nchA, dm, false, g0, nt)) { ok = false; break; }
+                if (!consume_group(true, p.seg_in, nchA, p.dm, false, g0, nt)) { ok = false; break; }
                 const uint32_t ew = tid < EPI_T ? reinterpret_cast<const uint32_t*>(smem + OFF_EPI)[tid] : 0u;
                 const uint32_t rA = ew & 0xFFFFFu;
                 if ((ew & EPI_OWN) && tiA >= g0 && tiA < g0 + nt && rA < p.proj) {
                     __half vh = __float2half_rn(reduce_item(tiA - g0, rowA, mA));
                     if (ew & EPI_CONV) {
-                        const uint32_t dA = rA - di;
+                        const uint32_t dA = rA - p.di;
                         // conv-state roll + depthwise conv + SiLU (k_conv_update_silu_split arithmetic)
                         const uint4 cv = *reinterpret_cast<const uint4*>(smem + OFF_CONV + tid * 16);
                         const __half* cvh = reinterpret_cast<const __half*>(&cv);
@@ -1023,7 +1014,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             {
                 if (tid < nslot * 64) {
                     const uint32_t sl = tid >> 6, w = tid & 63, key = skey[sl], m = key / p.G, g = key % p.G;
-                    const uint64_t* a = p.mb_in + (uint64_t)m * p.proj + 2 * di + (w < 32 ? 0 : GN) + g * p.N +
+                    const uint64_t* a = p.mb_in + (uint64_t)m * p.proj + 2 * p.di + (w < 32 ? 0 : GN) + g * p.N +
                                         (w & 31) * 4;
                     uint64_t v[4];
                     mb_ld2(a, v[0], v[1]);
@@ -1038,7 +1029,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                     // x and z of the row came from this CTA's own in_proj epilogue (rv[3], rv[4])
                     const uint32_t info = reinterpret_cast<const uint32_t*>(rowv)[tid * 6 + 5];
                     const uint32_t m = info >> 24, h = info & 0xFFFF;
-                    const uint64_t* adt = p.mb_in + (uint64_t)m * p.proj + di + p.xd + h;   // dt (raw)
+                    const uint64_t* adt = p.mb_in + (uint64_t)m * p.proj + p.di + p.xd + h;   // dt (raw)
                     uint64_t wdt = mb_ld(adt);
                     const float A = -expf(__half2float(L.A_log[h]));
                     const float dtb = __half2float(L.dt_bias[h]), Dh = __half2float(L.D[h]);
@@ -1095,7 +1086,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
                         *reinterpret_cast<float4*>(sstate + (uint64_t)j * p.N + lane * 4) = v2[q];
                         if (lane == 0) {
                             const float yh = __half2float(__float2half_rn(a2[q] + rv[2] * rv[3]));
-                            p.gated[(uint64_t)m * di + h * p.P + pp] = __float2half_rn(silu(rv[4]) * yh);
+                            p.gated[(uint64_t)m * p.di + h * p.P + pp] = __float2half_rn(silu(rv[4]) * yh);
                         }
                     }
                 }
@@ -1108,7 +1099,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             cons_sync();
             if (tid == 0 && urows) {
                 for (uint32_t m = 0; m < NB; ++m)
-                    bulk_s2g(L.ssd_state + ((uint64_t)m * di + 8 * tt.ub) * p.N,
+                    bulk_s2g(L.ssd_state + ((uint64_t)m * p.di + 8 * tt.ub) * p.N,
                              smem_u32(smem + OFF_S + m * urows * p.N * 4), urows * p.N * 4);
                 bulk_commit();
             }
@@ -1120,9 +1111,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
             }
             stamp(lb + 5);
             // ---- C: RMSNorm(gated), out_proj (tile, chunk) units -> out_proj slots
-            stage_norm(p.gated, di, nullptr, nullptr, L.mixer_norm_w, NB, di, true, xbuf, xsum, red);
+            stage_norm(p.gated, p.di, nullptr, nullptr, L.mixer_norm_w, NB, p.di, true, xbuf, xsum, red);
             stamp(lb + 6);
-            if (!gemv_phase(seg_out, nchC, di, dm, nuC, p.opart)) { ok = false; break; }
+            if (!gemv_phase(p.seg_out, nchC, p.di, p.dm, nuC, p.opart)) { ok = false; break; }
             stamp(lb + 7);
 
             if (!grid_sync(p, gen, abort)) { ok = false; break; }
@@ -1130,13 +1121,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
         if (!ok) break;
         // ---- residual + norm_f + lm_head + first-max argmax partials
         wait_ns = 0;
-        stage_norm_h<NB>(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, dm, false, xbuf, xsum, red);
+        stage_norm_h<NB>(p.opart, nchC, nullptr, p.embed, hid, p.norm_f, p.dm, false, xbuf, xsum, red);
         stamp(lmb + 0);
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
         for (uint32_t g0 = 0; g0 < ntL && ok; g0 += TG) {
             const uint32_t nt = min(TG, ntL - g0);
-            if (!consume_group(false, seg_lm, nchL, dm, false, g0, nt)) { ok = false; break; }
+            if (!consume_group(false, p.seg_lm, nchL, p.dm, false, g0, nt)) { ok = false; break; }
             if (tid < nt * 16 * NB) {
                 const uint32_t ti = tid / (16 * NB), row = (tid / NB) % 16, m = tid % NB;
                 const uint32_t r = (cta + (g0 + ti) * G) * 16 + row;
@@ -1204,18 +1195,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persist(PParams p) {
 cudaError_t launch_decode_persist(const PParams& prm, int sm_count, cudaStream_t s) {
     if (prm.B < 1 || prm.B > 2) return cudaErrorInvalidValue;
     const bool tr = prm.trace != nullptr;
-    const bool s5 = prm.seg_in == 5 && prm.seg_out == 5 && prm.seg_lm == 5;
-    const bool s27 = s5 && prm.dm == 2560 && prm.di == 5120;   // the 2.7B shape: a kernel of its own
-    const void* fn;
-    if (prm.B == 1) {
-        if (s27) fn = tr ? (const void*)k_decode_persist<1, true, 5, 2560> : (const void*)k_decode_persist<1, false, 5, 2560>;
-        else if (s5) fn = tr ? (const void*)k_decode_persist<1, true, 5, 0> : (const void*)k_decode_persist<1, false, 5, 0>;
-        else fn = tr ? (const void*)k_decode_persist<1, true, 0, 0> : (const void*)k_decode_persist<1, false, 0, 0>;
-    } else {
-        if (s27) fn = tr ? (const void*)k_decode_persist<2, true, 5, 2560> : (const void*)k_decode_persist<2, false, 5, 2560>;
-        else if (s5) fn = tr ? (const void*)k_decode_persist<2, true, 5, 0> : (const void*)k_decode_persist<2, false, 5, 0>;
-        else fn = tr ? (const void*)k_decode_persist<2, true, 0, 0> : (const void*)k_decode_persist<2, false, 0, 0>;
-    }
+    const void* fn = prm.B == 1 ? (tr ? (const void*)k_decode_persist<1, true> : (const void*)k_decode_persist<1, false>)
+                                : (tr ? (const void*)k_decode_persist<2, true> : (const void*)k_decode_persist<2, false>);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
