@@ -147,6 +147,10 @@ int lssm_plan_int4_gemm(uint32_t M, uint32_t N, uint32_t K, int sms, size_t ws_b
  * out[5] = {m tile, n tile, split, first K block, end K block}. */
 void lssm_int4_gemm_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint32_t splits, uint32_t nk,
                          uint32_t* out);
+/* The in_proj work of the persistent decode kernel for CTA s of G, computed by the function the
+ * kernel uses: out[4] = {first channel unit (8 d_inner channels), units, first B / C / dt tile,
+ * B / C / dt tiles (tile k = first + i * G)}. A CTA holding a B / C / dt tile is charged two units. */
+void lssm_persist_in_deal(uint32_t s, uint32_t G, uint32_t d_inner, uint32_t n_spec, uint32_t* out);
 /* Batched-decode extensions (no MetalOps counterpart): the GEMVs above take one activation
  * row (dims.M == 1, the checks of ops.mm:207-212 and :323-324); these take 1 <= dims.M <= 8 rows
  * (the sequences of one decode step, row-major (M, K) in, (M, N) out) and read the weights once

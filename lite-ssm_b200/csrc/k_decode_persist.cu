@@ -1297,3 +1297,13 @@ bool decode_persist_encode_maps(void* out, const PLayer* layers, const void* lm_
 }
 
 }  // namespace lssm
+
+// The in_proj work the persistent decode kernel deals to CTA s of G (the same function the
+// kernel calls): out = {first unit, units, first B / C / dt tile, B / C / dt tiles}.
+extern "C" void lssm_persist_in_deal(uint32_t s, uint32_t G, uint32_t d_inner, uint32_t n_spec, uint32_t* out) {
+    const lssm::InTiles t = lssm::in_tiles(s, G, d_inner, n_spec);
+    out[0] = t.ub;
+    out[1] = t.nu;
+    out[2] = t.kfirst;
+    out[3] = t.nsp;
+}

@@ -149,6 +149,7 @@ _OTHER = {
     "lssm_parse_header": (C.c_int, [P, sz, C.POINTER(HParams), C.POINTER(u32), C.c_char_p, sz]),
     "lssm_plan_int4_gemm": (C.c_int, [u32, u32, u32, C.c_int, sz, C.POINTER(u32), C.POINTER(u32)]),
     "lssm_int4_gemm_unit": (None, [u32, u32, u32, u32, u32, C.POINTER(u32)]),
+    "lssm_persist_in_deal": (None, [u32, u32, u32, u32, C.POINTER(u32)]),
 }
 
 _lib = None
