@@ -151,6 +151,10 @@ void lssm_int4_gemm_unit(uint32_t tile, uint32_t m_tiles, uint32_t n_tiles, uint
  * kernel uses: out[4] = {first channel unit (8 d_inner channels), units, first B / C / dt tile,
  * B / C / dt tiles (tile k = first + i * G)}. A CTA holding a B / C / dt tile is charged two units. */
 void lssm_persist_in_deal(uint32_t s, uint32_t G, uint32_t d_inner, uint32_t n_spec, uint32_t* out);
+/* The N tile (128, 144, 160, 192, 240 or 256 columns) the fp16 tensor-core GEMM (lssm_linear_f16_gemm,
+ * and the INT4 GEMM's dequantise-then-GEMM path) picks for an M x N output on `sms` SMs, computed by the
+ * launcher's own function: the fill of the last persistent wave weighed by the shared-memory operand rate. */
+int lssm_plan_gemm_f16(uint32_t M, uint32_t N, int sms);
 /* Batched-decode extensions (no MetalOps counterpart): the GEMVs above take one activation
  * row (dims.M == 1, the checks of ops.mm:207-212 and :323-324); these take 1 <= dims.M <= 8 rows
  * (the sequences of one decode step, row-major (M, K) in, (M, N) out) and read the weights once

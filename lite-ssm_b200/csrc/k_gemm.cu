@@ -325,21 +325,11 @@ static int sm_count() {
     return n;
 }
 
-cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, uint32_t N, uint32_t K, int epilogue,
-                            cudaStream_t s) {
-    if (!M || !N || !K) return cudaSuccess;
-    const bool tma_ok = (K % 8 == 0) && aligned(x, 16) && aligned(w, 16);
-    if (!tma_ok) {
-        dim3 grid((N + 63) / 64, (M + 63) / 64);
-        k_gemm_simt<<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(w),
-                                         static_cast<__half*>(y), M, N, K, epilogue);
-        return cudaGetLastError();
-    }
-    // N tile: the share of SM-slots the persistent waves fill, times a shared-memory factor. At
-    // M = 128 one K = 16 MMA reads 4 KB of A and 32 * BN bytes of B in ~0.52 * BN cycles, so
-    // narrow tiles need more operand bytes per cycle than shared memory sustains (~100 of the
-    // nominal 128 B / cycle): 128 -> 123, 160 -> 111, 192 -> 102, 256 -> 92 B / cycle.
-    const int sms = sm_count();
+// N tile of the fp16 GEMM: the share of SM-slots the persistent waves fill, times a shared-memory
+// factor. At M = 128 one K = 16 MMA reads 4 KB of A and 32 * BN bytes of B in ~0.52 * BN cycles, so
+// narrow tiles need more operand bytes per cycle than shared memory sustains (~100 of the nominal
+// 128 B / cycle): 128 -> 123, 144 -> 116, 160 -> 111, 192 -> 102, 240 -> 94, 256 -> 92 B / cycle.
+int gemm_f16_tile_n(uint32_t M, uint32_t N, int sms) {
     const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
     double best = -1.0;
     int best_bn = 256;
@@ -352,6 +342,21 @@ cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, u
         const double score = eff * (bpc > 100.0 ? 100.0 / bpc : 1.0);
         if (score > best + 1e-9) { best = score; best_bn = c; }
     }
+    return best_bn;
+}
+
+cudaError_t launch_gemm_f16(const void* x, const void* w, void* y, uint32_t M, uint32_t N, uint32_t K, int epilogue,
+                            cudaStream_t s) {
+    if (!M || !N || !K) return cudaSuccess;
+    const bool tma_ok = (K % 8 == 0) && aligned(x, 16) && aligned(w, 16);
+    if (!tma_ok) {
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        k_gemm_simt<<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(w),
+                                         static_cast<__half*>(y), M, N, K, epilogue);
+        return cudaGetLastError();
+    }
+    const int sms = sm_count();
+    const int best_bn = gemm_f16_tile_n(M, N, sms);
     if (best_bn == 256) return run_gemm_tc<256>(x, w, y, M, N, K, epilogue, sms, s);
     if (best_bn == 192) return run_gemm_tc<192>(x, w, y, M, N, K, epilogue, sms, s);
     if (best_bn == 240) return run_gemm_tc<240>(x, w, y, M, N, K, epilogue, sms, s);
@@ -429,3 +434,6 @@ cudaError_t launch_int4_dequant_f16(const void* packed, const void* scales, void
 }
 
 }  // namespace lssm
+
+// The N tile the fp16 GEMM launcher picks for an M x N output on `sms` SMs (its own function).
+extern "C" int lssm_plan_gemm_f16(uint32_t M, uint32_t N, int sms) { return lssm::gemm_f16_tile_n(M, N, sms); }

@@ -150,6 +150,7 @@ _OTHER = {
     "lssm_plan_int4_gemm": (C.c_int, [u32, u32, u32, C.c_int, sz, C.POINTER(u32), C.POINTER(u32)]),
     "lssm_int4_gemm_unit": (None, [u32, u32, u32, u32, u32, C.POINTER(u32)]),
     "lssm_persist_in_deal": (None, [u32, u32, u32, u32, C.POINTER(u32)]),
+    "lssm_plan_gemm_f16": (C.c_int, [u32, u32, C.c_int]),
 }
 
 _lib = None

@@ -90,3 +90,30 @@ def test_split_needs_room_for_two_partials():
     M, N, K = 64, 10576, 2560
     assert plan(M, N, K, 2 * M * N * 4)[2] >= 2
     assert plan(M, N, K, 2 * M * N * 4 - 16)[2] == 1
+
+
+# ---------------------------------------------------------------------------
+# fp16 tensor-core GEMM: the N tile the launcher picks (lssm_plan_gemm_f16, its own function)
+def tile_f16(M, N, sms=SMS):
+    return lssm.lib().lssm_plan_gemm_f16(M, N, sms)
+
+
+def test_f16_gemm_tiles_of_the_2p7b_prefill():
+    """2048-token prefill: in_proj (N 10576) takes 240-wide tiles (720 tiles = 4.86 waves on 148 SMs;
+    256 would leave 672 = 4.54 waves), out_proj (N 2560) 144-wide ones (288 tiles = 1.95 waves; 160
+    gives 256 = 1.73)."""
+    assert tile_f16(2048, 10576) == 240
+    assert tile_f16(2048, 2560) == 144
+
+
+@pytest.mark.parametrize("M,N", [(2048, 10576), (2048, 2560), (512, 1024), (200, 300), (16384, 2320), (16384, 4096),
+                                 (1, 16), (4096, 18560)])
+def test_f16_gemm_tile_is_a_compiled_width_with_best_fill(M, N):
+    bn = tile_f16(M, N)
+    assert bn in (128, 144, 160, 192, 240, 256)
+    # no other width fills the persistent waves better without a lower shared-memory factor
+    def fill(c):
+        tiles = -(-M // 128) * -(-N // c)
+        waves = -(-tiles // SMS)
+        return M * N / (waves * SMS * 128 * c)
+    assert fill(bn) >= 0.8 * max(fill(c) for c in (128, 144, 160, 192, 240, 256))
