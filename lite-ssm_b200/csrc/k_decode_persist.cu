@@ -232,23 +232,8 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t seg, uint32_t s, ui
     return line * 128 + ((j ^ (line & 7)) << 4);
 }
 
-// Bias-folding dequantisation of one packed word (nibbles u = q + 8 of k0..k7, q signed) into
-// the MMA pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), with one shift: the even nibbles k0 / k4 and
-// (after w >> 8) k2 / k6 sit in bits 0..3 of their fp16 lanes and are written under the
-// exponent of 1024 (unit 1 there), the odd ones sit in bits 4..7 and are written under the
-// exponent of 64 (unit 1 there). The values are exact: 1032 + q for even k, 72 + q for odd
-// k, so a block's dot product with x equals sum(q * x) + 1032 * sum(x_even) + 72 * sum(x_odd)
-// and the caller starts the accumulator at minus that bias. 5 instructions per word.
-__device__ __forceinline__ void dequant_word_fold2(uint32_t w, uint32_t q[4]) {
-    const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, M1024 = 0x64086408u, M64 = 0x54805480u;
-    const uint32_t w8 = w >> 8;
-    q[0] = lop3_6a(w, LO, M1024);
-    q[1] = lop3_6a(w, HI, M64);
-    q[2] = lop3_6a(w8, LO, M1024);
-    q[3] = lop3_6a(w8, HI, M64);
-}
-// Accumulator start of a block from its {even, odd} activation sums.
-__device__ __forceinline__ float fold_bias(float2 s) { return fmaf(-1032.0f, s.x, -72.0f * s.y); }
+// Accumulator start of a block from its {even, odd} activation sums (dequant_word_fold's bias).
+__device__ __forceinline__ float fold_bias(float2 s) { return lssm::fold_bias(s.x, s.y); }
 
 // Two k16 MMAs of one 32-wide block j of a segment line (rows g and g + 8), the B fragment
 // (bx, by | bz, bw) supplied by the caller.
@@ -257,8 +242,8 @@ __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint3
     const uint32_t wa = *reinterpret_cast<const uint32_t*>(ra + off);
     const uint32_t wb = *reinterpret_cast<const uint32_t*>(ra + rb8 + off);
     uint32_t qa[4], qb[4];
-    dequant_word_fold2(wa, qa);
-    dequant_word_fold2(wb, qb);
+    dequant_word_fold(wa, qa);
+    dequant_word_fold(wb, qb);
     const uint32_t a1[4] = {qa[0], qb[0], qa[1], qb[1]};
     const uint32_t a2[4] = {qa[2], qb[2], qa[3], qb[3]};
     mma_16816(da, a1, bx, by);
@@ -272,7 +257,7 @@ __device__ __forceinline__ void mma_block(const uint8_t* ra, uint32_t rb8, uint3
 // column 2j + m is block 8s + 4h + j of sequence m. Only the lanes of a column's group
 // supply that block's activation fragment (the others zero), so column n ends up holding
 // sum_k W[row][k] x_n[k] of its block alone and the scales are applied once per column.
-// The weights use the bias-folded dequantisation (dequant_word_fold2); the folded bias of each
+// The weights use the bias-folded dequantisation (dequant_word_fold); the folded bias of each
 // block is cancelled by starting the accumulator at fold_bias of its activation sums.
 // acc: rows g / g + 8 (one sequence: acc[0] / acc[2]; two: acc[0..1] / acc[2..3] per m).
 __device__ __forceinline__ void consume_int4(const uint8_t* stage, uint32_t seg, uint32_t chunk, const uint4* xs,

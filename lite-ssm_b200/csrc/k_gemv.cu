@@ -118,7 +118,7 @@ __device__ __forceinline__ void stage_x_vec(const __half* __restrict__ x, const 
 
 // Staging for the bias-folded INT4 MMA (dequant_word_fold): one thread per (row m,
 // 32-k block b) writes the block's four fragment quads and corr[b * cs + m] =
-// -72 * sum(x over the block), summed in a fixed order (deterministic). cs = 8: rows
+// fold_bias(sum of x at even k, sum at odd k) over the block, summed in a fixed order (deterministic). cs = 8: rows
 // m in [M, 8) get corr 0 (multi-row MMA columns); cs = 1: one row. x values as in_val
 // (RMS-normalised with rr when nw is given).
 __device__ __forceinline__ void stage_x_fold(const __half* __restrict__ x, const __half* __restrict__ nw, uint32_t M,
@@ -151,7 +151,7 @@ __device__ __forceinline__ void stage_x_fold(const __half* __restrict__ x, const
             corr[b * cs + m] = 0.0f;
             continue;
         }
-        float sx = 0.0f;
+        float se = 0.0f, so = 0.0f;
 #pragma unroll
         for (uint32_t o = 0; o < 4; ++o) {
             const uint32_t q = b * 4 + o;
@@ -166,7 +166,10 @@ __device__ __forceinline__ void stage_x_fold(const __half* __restrict__ x, const
                 for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(__half2float(v[j]) * __half2float(w8[j]) * r);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) sx += __half2float(v[j]);
+            for (int j = 0; j < 8; j += 2) {
+                se += __half2float(v[j]);
+                so += __half2float(v[j + 1]);
+            }
             const __half2 o0 = __halves2half2(v[0], v[4]), o1 = __halves2half2(v[1], v[5]);
             const __half2 o2 = __halves2half2(v[2], v[6]), o3 = __halves2half2(v[3], v[7]);
             uint4 f;
@@ -176,7 +179,7 @@ __device__ __forceinline__ void stage_x_fold(const __half* __restrict__ x, const
             f.w = *reinterpret_cast<const uint32_t*>(&o3);
             xs[(uint64_t)m * nq + q] = f;
         }
-        corr[b * cs + m] = -72.0f * sx;
+        corr[b * cs + m] = fold_bias(se, so);
     }
 }
 
@@ -497,10 +500,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_int4_mma(const __half* __
 //  load block j's weight words (16 rows x 32 k) as the A fragment, and only the lanes
 //  of group g == j supply the activation fragment (the others give zeros), so after
 //  the group D[row][j] is block j's dot product. The bias folding of
-//  dequant_word_fold starts column j at corr[j] (-72 x the block's sum of x), and the
+//  dequant_word_fold starts column j at corr[j] (fold_bias of the block's x), and the
 //  per-block scales are applied once per group in the epilogue (lane (g, c) owns
 //  columns 2c, 2c + 1): per block 2 shared loads of weight words, one predicated
-//  fragment load, 14 dequant ops and 2 MMAs.
+//  fragment load, 10 dequant ops and 2 MMAs.
 //  wa / wb: row g / g + 8 weight word of block b at wa[b * 4]; sa / sb: their scales;
 //  xq: the fragment quads of this lane's c (block b at xq[b * 4]); corr[b] biases.
 // ---------------------------------------------------------------------------

@@ -41,20 +41,26 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t q[4]) {
     q[3] = *reinterpret_cast<uint32_t*>(&h3);
 }
 
-// Bias-folding dequantisation: every nibble is moved to bits 4..7 of its fp16 lane
-// (w << 4, w, w >> 4, w >> 8) and one lop3 per pair writes (nib ^ 8) there under the
-// exponent of 64.0, giving the exact values 64 + u, u = nib ^ 8 = q + 8, in the pairs
-// (k0,k4) (k1,k5) (k2,k6) (k3,k7). A dot product with x over them equals
-// sum(q * x) + 72 * sum(x): the caller starts the MMA accumulator at -72 * sum(x) of
-// the block. 7 instructions per word (3 shifts + 4 lop3) instead of dequant_word's 9,
-// and the folded bias is only 72x the activation, so the fp32 accumulation keeps the
-// products' precision.
+// Bias-folding dequantisation of one packed word (nibbles u = q + 8 of k0..k7, q signed) into the
+// MMA pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7) with one shift: the even nibbles k0 / k4 and (after
+// w >> 8) k2 / k6 sit in bits 0..3 of their fp16 lanes and are written under the exponent of 1024
+// (unit 1 there), the odd ones sit in bits 4..7 and are written under the exponent of 64 (unit 1
+// there). The values are exact: 1032 + q for even k, 72 + q for odd k, so a block's dot product
+// with x equals sum(q * x) + 1032 * sum(x_even) + 72 * sum(x_odd): the caller starts the MMA
+// accumulator at fold_bias of the block's even / odd activation sums. 5 instructions per word
+// (dequant_word: 9). The folded bias stays small next to fp32's 24 bits, so the products keep
+// their precision.
 __device__ __forceinline__ void dequant_word_fold(uint32_t w, uint32_t q[4]) {
-    const uint32_t HI = 0x00F000F0u, M64 = 0x54805480u;
-    q[0] = lop3_6a(w << 4, HI, M64);
+    const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, M1024 = 0x64086408u, M64 = 0x54805480u;
+    const uint32_t w8 = w >> 8;
+    q[0] = lop3_6a(w, LO, M1024);
     q[1] = lop3_6a(w, HI, M64);
-    q[2] = lop3_6a(w >> 4, HI, M64);
-    q[3] = lop3_6a(w >> 8, HI, M64);
+    q[2] = lop3_6a(w8, LO, M1024);
+    q[3] = lop3_6a(w8, HI, M64);
+}
+// Accumulator start of a block from its {even k, odd k} activation sums.
+__device__ __forceinline__ float fold_bias(float even_sum, float odd_sum) {
+    return fmaf(-1032.0f, even_sum, -72.0f * odd_sum);
 }
 
 // D += A(16x16, f16) * B(16x8, f16), fp32 accumulate.
